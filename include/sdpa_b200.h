@@ -1,0 +1,104 @@
+/*
+ * sdpa_b200 -- C ABI of the Blackwell (sm_100a) scaled-dot-product attention
+ * forward / backward behind the reference's TensorFlow ops `Sdpa` and
+ * `SdpaGrad`.
+ *
+ * The entry points replace the reference's device-functor seam:
+ *   sdpa_b200_fwd  <- functor::FlashAttnFunctor<GPUDevice,T>::operator()
+ *                     (sdpa/sdpa.h:11-17, sdpa/sdpa_fwd.cu.cc:176-240),
+ *                     called from SdpaFwdOp::Compute (sdpa/sdpa_cpu.cc:84-86)
+ *   sdpa_b200_bwd  <- functor::FlashAttnGradFunctor<GPUDevice,T>::operator()
+ *                     (sdpa/sdpa.h:19-33, sdpa/sdpa_bwd.cu.cc:347-453),
+ *                     called from SdpaBwdOp::Compute (sdpa/sdpa_cpu.cc:188-191)
+ *
+ * Conventions
+ *   - Tensors are dense row-major [B, S, D] (B = batch x heads folded),
+ *     device pointers; stats is float32 [B, S_q] in natural-log units:
+ *     stats = max_j(scale*q.k_j) + ln(sum_j exp(scale*q.k_j - max) + 1e-6).
+ *   - dtype: SDPA_B200_F16 (IEEE half) or SDPA_B200_F32.
+ *   - Dropout: element (b,i,j) is dropped iff hi32(LCG(seed + offset +
+ *     (b*S_q + i)*S_kv + j)) / 2^32 < dropout, enabled iff dropout > 1e-6
+ *     (sdpa/sdpa_utils.cuh:13-19, sdpa/sdpa_fwd.cu.cc:136).  Kept
+ *     probabilities are scaled by 1/(1 - dropout).
+ *   - causal != 0 masks j > i and requires S_q == S_kv.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream), never allocates, frees or synchronises, and is
+ *     reentrant.  The caller owns every buffer.
+ *   - Return value: SDPA_B200_OK or an error code; sdpa_b200_strerror() gives
+ *     text.  Errors never abort the process.
+ */
+#ifndef SDPA_B200_H_
+#define SDPA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum sdpa_b200_dtype { SDPA_B200_F16 = 0, SDPA_B200_F32 = 1 };
+
+enum sdpa_b200_status {
+  SDPA_B200_OK = 0,
+  SDPA_B200_EINVAL = 1,       /* bad shape, dtype, pointer or argument        */
+  SDPA_B200_EUNSUPPORTED = 2, /* max(D_qk, D_v) > 128                          */
+  SDPA_B200_ECUDA = 3,        /* a CUDA runtime / launch error                 */
+  SDPA_B200_ETIMEOUT = 4,     /* a device-side wait gave up (see status word)  */
+  SDPA_B200_EWORKSPACE = 5    /* workspace missing or too small                */
+};
+
+/* Forward: out [B,S_q,D_v] (dtype), stats [B,S_q] float32.
+ * Replaces FlashAttnFunctor<GPUDevice,T> (sdpa/sdpa_fwd.cu.cc:176-240). */
+int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
+                  int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
+                  uint64_t seed, uint64_t offset, void* stream);
+
+/* Scratch the backward needs: one float32 per query row (rowsum(dO*O)).
+ * The caller allocates it (TF: allocate_temp). */
+size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v);
+
+/* Backward: dq, dk, dv shaped like q, k, v (dtype), from q, k, v, out, stats
+ * and d_out of the forward.  Two kernels, dK/dV then dQ, no atomics.
+ * Replaces FlashAttnGradFunctor<GPUDevice,T> (sdpa/sdpa_bwd.cu.cc:347-453). */
+int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                  const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
+                  int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Writes mask[b][i][j] = 1 where (b,i,j) is dropped, from the same device RNG
+ * routine the kernels use (diagnostic; no reference counterpart beyond the
+ * RNG of sdpa/sdpa_utils.cuh:13-19).  mask is a device uint8 [B,S_q,S_kv]. */
+int sdpa_b200_dropout_mask(uint64_t seed, uint64_t offset, int64_t B, int64_t S_q, int64_t S_kv, float dropout,
+                           uint8_t* mask, void* stream);
+
+/* Text for a status code. */
+const char* sdpa_b200_strerror(int status);
+
+/* Device status word of the current device: bit 0 = a bounded wait timed out
+ * inside a kernel.  Synchronises `stream`, reads the word and clears it. */
+int sdpa_b200_device_status(unsigned int* word, void* stream);
+
+/* Bound (nanoseconds) of every device-side wait; 0 restores the default (2 s). */
+void sdpa_b200_set_wait_timeout_ns(uint64_t ns);
+
+/* Diagnostic: launches one CTA that waits on an mbarrier nothing arrives at,
+ * bounded by timeout_ns; the wait gives up and raises bit 0 of the status
+ * word.  Used to test timeout handling without faulting the GPU. */
+int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/* Which kernel family serves a shape: 1 = tcgen05 tensor-core kernels,
+ * 0 = SIMT kernels (head dims whose rows are not 16-byte multiples, or
+ * forced by SDPA_B200_FORCE_SIMT=1). */
+int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward);
+
+/* Number of kernel launches the last successful fwd/bwd call on this thread made. */
+int sdpa_b200_last_launch_count(void);
+
+/* ABI version (major*100 + minor). */
+int sdpa_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SDPA_B200_H_ */

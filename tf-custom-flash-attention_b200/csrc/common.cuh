@@ -1,0 +1,64 @@
+// Parameters shared by every kernel of the library.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace sdpa_b200 {
+
+constexpr float kEps = 1e-6f;        // sdpa/sdpa_utils.cuh:9
+constexpr float kNegInit = -1e9f;    // initial running max, sdpa/sdpa_utils.cuh:11
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct Params {
+  // inputs
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;        // backward: forward output
+  const void* d_o;      // backward: gradient of the output
+  const float* lse;     // backward: stats of the forward (natural log)
+  float* delta;         // backward workspace: rowsum(dO*O), [B*S_q]
+  // outputs
+  void* out;
+  float* stats;
+  void* dq;
+  void* dk;
+  void* dv;
+  // shape
+  int64_t B, S_q, S_kv;
+  int D_qk, D_v;
+  // semantics
+  float scale;          // as given
+  float scale_log2;     // scale * log2(e)
+  int causal;
+  int dropout_on;       // dropout > 1e-6
+  float dp_inv;         // 1 / (1 - dropout) (1 when off)
+  float dp_keep;        // 1 / dp_inv  ( = 1 - dropout in fp32, as D_i / dp_inverse)
+  uint64_t drop_thr;    // dropped iff hi32(state) < drop_thr
+  uint64_t rng_base;    // seed + offset
+  uint64_t timeout_ns;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<float>(float x) {
+  return x;
+}
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) {
+  return __half2float(x);
+}
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <>
+__device__ __forceinline__ float from_f<float>(float x) {
+  return x;
+}
+template <>
+__device__ __forceinline__ __half from_f<__half>(float x) {
+  return __float2half_rn(x);
+}
+
+}  // namespace sdpa_b200

@@ -1,0 +1,369 @@
+// Forward attention on the 5th-generation tensor cores (sm_100a), fp16 in,
+// fp32 accumulate.  One CTA = one 128-row query tile of one batch row.
+//
+//   warp 4      TMA producer: Q once, then K/V tiles (128 keys) into a
+//               2-stage ring of 128B-swizzled shared-memory buffers
+//   warp 5      MMA issuer (one thread) + TMEM owner:
+//                 S[j%2] = Q K_j^T           (SS MMA, 128x128, K = D_qk)
+//                 O     += P_{j-1} V_{j-1}   (TS MMA, A = P read from TMEM)
+//   warps 0-3   softmax: thread t owns query row t = TMEM lane t.  Reads its
+//               S row (128 fp32) from TMEM, masks, online max in log2 units
+//               with scale folded into the exponent, exp2, row sum, dropout,
+//               writes P (fp16 pairs) back over S, rescales O only when the
+//               running max grew by more than 2^8 (exact: the final division
+//               uses the same reference max), then the epilogue.
+//
+// TMEM columns: [0,128) S0/P0, [128,256) S1/P1, [256,256+DV) O.
+// Semantics follow sdpa/sdpa_fwd.cu.cc:60-173: l sums pre-dropout p,
+// stats = max + ln(l + 1e-6), O = acc / l guarded by l > 1e-6.
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace sdpa_b200 {
+namespace tc {
+
+constexpr int kBM = 128;  // query rows per CTA (= TMEM lanes)
+constexpr int kBN = 128;  // keys per tile
+constexpr int kFwdThreads = 192;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int DQK, int DV>
+struct FwdCfg {
+  static constexpr int kStages = 2;
+  static constexpr uint32_t kQBytes = kBM * DQK * 2;
+  static constexpr uint32_t kKBytes = kBN * DQK * 2;
+  static constexpr uint32_t kVBytes = kBN * DV * 2;
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kKOff = kQOff + kQBytes;
+  static constexpr uint32_t kVOff = kKOff + kStages * kKBytes;
+  static constexpr uint32_t kBarOff = kVOff + kStages * kVBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;  // + barriers + alignment slack
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(256 + DV <= 512, "TMEM budget");
+};
+
+struct FwdBarriers {
+  uint64_t q_full;
+  uint64_t k_full[2];
+  uint64_t v_full[2];
+  uint64_t kv_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Warp-uniform bounded wait: every lane spins until all lanes observed the
+// phase; the give-up decision is taken by lane 0 and broadcast, so the warp
+// never diverges in front of a .sync.aligned instruction.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtl& ctl) {
+  bool done = mbar_try_wait(bar, parity);
+  uint32_t spins = 0;
+  while (!__all_sync(0xffffffffu, done)) {
+    if (!done) done = mbar_try_wait(bar, parity);
+    if ((++spins & 255u) == 0) {
+      int give_up = 0;
+      if ((threadIdx.x & 31) == 0) give_up = (*ctl.abort_flag) || (globaltimer_ns() > ctl.deadline_ns);
+      give_up = __shfl_sync(0xffffffffu, give_up, 0);
+      if (give_up) {
+        if ((threadIdx.x & 31) == 0) {
+          *ctl.abort_flag = 1;
+          atomicOr(&g_status_word, kStatusTimeout);
+        }
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
+  const uint32_t a = smem_u32(raw);
+  return raw + ((1024u - (a & 1023u)) & 1023u);
+}
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using Cfg = FwdCfg<DQK, DV>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(smem + Cfg::kBarOff);
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+
+  const int64_t n_qt = (p.S_q + kBM - 1) / kBM;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
+  const int64_t m0 = qt * kBM;
+  const int64_t n_kv_all = (p.S_kv + kBN - 1) / kBN;
+  const int n_kv = static_cast<int>(p.causal ? min(n_kv_all, qt + 1) : n_kv_all);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->p_full[s], kBM);
+    }
+    mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->mma_done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  WaitCtl ctl;
+  ctl.deadline_ns = globaltimer_ns() + p.timeout_ns;
+  ctl.abort_flag = &bars->abort_flag;
+
+  const uint32_t sQ = smem_u32(smem + Cfg::kQOff);
+  const uint32_t sK0 = smem_u32(smem + Cfg::kKOff);
+  const uint32_t sV0 = smem_u32(smem + Cfg::kVOff);
+
+  if (warp == 4) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_expect_tx(&bars->q_full, Cfg::kQBytes);
+#pragma unroll
+      for (int c = 0; c < DQK / 64; ++c)
+        tma_load_3d(smem + Cfg::kQOff + c * kBM * 128, &tm_q, c * 64, static_cast<int>(m0), static_cast<int>(b),
+                    &bars->q_full);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&bars->kv_empty[s], ((j >> 1) & 1) ^ 1, ctl)) break;
+        uint8_t* kdst = smem + Cfg::kKOff + s * Cfg::kKBytes;
+        uint8_t* vdst = smem + Cfg::kVOff + s * Cfg::kVBytes;
+        mbar_expect_tx(&bars->k_full[s], Cfg::kKBytes);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(kdst + c * kBN * 128, &tm_k, c * 64, j * kBN, static_cast<int>(b), &bars->k_full[s]);
+        mbar_expect_tx(&bars->v_full[s], Cfg::kVBytes);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(vdst + c * kBN * 128, &tm_v, c * 64, j * kBN, static_cast<int>(b), &bars->v_full[s]);
+        issued = j + 1;
+      }
+      if (*ctl.abort_flag) {
+        // Let the copies already in flight land before the CTA exits.
+        WaitCtl drain = ctl;
+        drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+        int dummy = 0;
+        drain.abort_flag = &dummy;
+        for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j) {
+          mbar_wait(&bars->k_full[j & 1], (j >> 1) & 1, drain);
+          mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, drain);
+        }
+        if (issued == 0) mbar_wait(&bars->q_full, 0, drain);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_qk = make_idesc(kBM, kBN, false, false, false);
+      constexpr uint32_t idesc_pv = make_idesc(kBM, DV, false, true, false);
+      const uint32_t tO = tmem + 256;
+      bool ok = mbar_wait(&bars->q_full, 0, ctl);
+      auto issue_pv = [&](int t) -> bool {
+        const int s = t & 1;
+        if (!mbar_wait(&bars->p_full[s], (t >> 1) & 1, ctl)) return false;
+        if (!mbar_wait(&bars->v_full[s], (t >> 1) & 1, ctl)) return false;
+        tc_fence_after();
+        const uint32_t vbase = sV0 + s * Cfg::kVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bdesc = make_sw128_desc(vbase + kk * 16 * 128, kBN * 128, 1024);
+          mma_f16_ts(tO, tmem + s * 128 + kk * 8, bdesc, idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&bars->kv_empty[s]);
+        mma_commit(&bars->o_done);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&bars->k_full[s], (j >> 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kbase = sK0 + s * Cfg::kKBytes;
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint64_t adesc = make_sw128_desc(sQ + koff, 16, 1024);
+          const uint64_t bdesc = make_sw128_desc(kbase + koff, 16, 1024);
+          mma_f16_ss(tmem + s * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&bars->s_full[s]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) issue_pv(n_kv - 1);
+      // Every MMA issued so far must finish before TMEM is released.
+      mma_commit(&bars->mma_done);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else {
+    // ------------------------------------------------ softmax warpgroup
+    const int t = threadIdx.x;  // 0..127 = TMEM lane = query row in tile
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int64_t row = m0 + t;
+    const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + row) * static_cast<uint64_t>(p.S_kv);
+    float m_run = -INFINITY;  // true running max (log2 units, scaled)
+    float m_use = -INFINITY;  // reference max the exponentials are taken against
+    float l = 0.0f;           // sum of exp2(x - m_use), pre-dropout
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, ctl)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[128];
+      SDPA_TMEM_LD32(tmem + lane_base + s * 128 + 0, (r + 0));
+      SDPA_TMEM_LD32(tmem + lane_base + s * 128 + 32, (r + 32));
+      SDPA_TMEM_LD32(tmem + lane_base + s * 128 + 64, (r + 64));
+      SDPA_TMEM_LD32(tmem + lane_base + s * 128 + 96, (r + 96));
+      tmem_wait_ld();
+      const int64_t kv0 = static_cast<int64_t>(j) * kBN;
+      int64_t lim64 = p.S_kv - kv0;
+      if (p.causal) lim64 = min(lim64, row - kv0 + 1);
+      const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kBN ? kBN : lim64));
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float x = (c < lim) ? __uint_as_float(r[c]) * p.scale_log2 : -INFINITY;
+        r[c] = __float_as_uint(x);
+        tmax = fmaxf(tmax, x);
+      }
+      m_run = fmaxf(m_run, tmax);
+      float alpha = 1.0f;
+      bool rescale_o = false;
+      if (tmax > m_use + kRescaleThreshold) {
+        alpha = ex2(m_use - m_run);  // 0 when m_use = -inf
+        rescale_o = (j > 0) && (m_use != -INFINITY);
+        m_use = m_run;
+        l *= alpha;
+      }
+      const float mu = (m_use == -INFINITY) ? 0.0f : m_use;
+      float rs = 0.0f;
+      uint32_t pk[64];
+      if (p.dropout_on) {
+        uint64_t st = lcg_state(rbase, static_cast<uint64_t>(kv0));
+#pragma unroll
+        for (int c = 0; c < 128; c += 2) {
+          float p0 = ex2(__uint_as_float(r[c]) - mu);
+          float p1 = ex2(__uint_as_float(r[c + 1]) - mu);
+          rs += p0 + p1;
+          if (dropped(st, p.drop_thr)) p0 = 0.0f;
+          st += kLcgA;
+          if (dropped(st, p.drop_thr)) p1 = 0.0f;
+          st += kLcgA;
+          pk[c / 2] = pack_half2(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; c += 2) {
+          const float p0 = ex2(__uint_as_float(r[c]) - mu);
+          const float p1 = ex2(__uint_as_float(r[c + 1]) - mu);
+          rs += p0 + p1;
+          pk[c / 2] = pack_half2(p0, p1);
+        }
+      }
+      l += rs;
+      SDPA_TMEM_ST32(tmem + lane_base + s * 128 + 0, (pk + 0));
+      SDPA_TMEM_ST32(tmem + lane_base + s * 128 + 32, (pk + 32));
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O must hold PV_{j-1} before it is rescaled (and before PV_j).
+        if (!warp_wait(&bars->o_done, (j - 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float a = rescale_o ? alpha : 1.0f;
+#pragma unroll
+        for (int c = 0; c < DV / 32; ++c) {
+          uint32_t o[32];
+          SDPA_TMEM_LD32(tmem + lane_base + 256 + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+          SDPA_TMEM_ST32(tmem + lane_base + 256 + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[s]);
+    }
+    // ----------------------------------------------------------- epilogue
+    if (ok && n_kv > 0) ok = warp_wait(&bars->o_done, (n_kv - 1) & 1, ctl);
+    if (ok) {
+      tc_fence_after();
+      float lse, inv;
+      if (m_run == -INFINITY) {
+        lse = kNegInit + logf(kEps);
+        inv = 0.0f;
+      } else {
+        const float l_true = l * ex2(m_use - m_run);  // sum relative to the true max
+        lse = m_run * kLn2 + logf(l_true + kEps);
+        inv = (l_true > kEps) ? p.dp_inv / l : 0.0f;
+      }
+      const bool active = row < p.S_q;
+      if (active) p.stats[b * p.S_q + row] = lse;
+      __half* orow = static_cast<__half*>(p.out) + (b * p.S_q + row) * p.D_v;
+#pragma unroll
+      for (int c = 0; c < DV / 32; ++c) {
+        uint32_t o[32];
+        if (n_kv > 0) {
+          SDPA_TMEM_LD32(tmem + lane_base + 256 + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        uint32_t h[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          h[e] = pack_half2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        if (active) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int col = c * 32 + w * 8;
+            if (col < p.D_v)
+              *reinterpret_cast<uint4*>(orow + col) = make_uint4(h[4 * w], h[4 * w + 1], h[4 * w + 2], h[4 * w + 3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace tc
+}  // namespace sdpa_b200

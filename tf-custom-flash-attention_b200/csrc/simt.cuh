@@ -1,0 +1,274 @@
+// SIMT kernels: the general path for shapes the tensor-core kernels do not
+// take (head-dim rows that are not a multiple of 16 bytes, hence not
+// TMA-addressable) and for fp32 until its tensor-core path serves it.
+// Same semantics as the tensor-core kernels (see api.cu); FP32 arithmetic.
+//   fwd      one thread per query row, K/V tiles staged in shared memory
+//   delta    one warp per query row: D_i = sum_d dO*O
+//   dkdv     one thread per key row, Q/dO tiles staged, K/V transposed in smem
+//   dq       one thread per query row, K/V tiles staged, Q/dO transposed in smem
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace sdpa_b200 {
+namespace simt {
+
+constexpr int kFwdRows = 128;  // query rows per CTA
+constexpr int kFwdKeys = 32;   // keys per staged tile
+constexpr int kBwdRows = 64;   // rows owned per CTA in dkdv / dq
+constexpr int kBwdTile = 32;   // rows per staged tile of the other side
+
+template <typename T>
+__device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t row0, int64_t nrows_total, int rows,
+                                           int D, int DM, int tid, int nthreads) {
+  // dst[r][d] (row-major, width DM) <- src rows row0.. (zero outside)
+  for (int idx = tid; idx < rows * DM; idx += nthreads) {
+    int r = idx / DM, d = idx - r * DM;
+    int64_t gr = row0 + r;
+    dst[idx] = (gr < nrows_total && d < D) ? to_f<T>(src[gr * D + d]) : 0.0f;
+  }
+}
+
+template <typename T, int DM>
+__global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
+  __shared__ float Ks[kFwdKeys * DM];
+  __shared__ float Vs[kFwdKeys * DM];
+  const int64_t n_qt = (p.S_q + kFwdRows - 1) / kFwdRows;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // heavy causal tiles first
+  const int tid = threadIdx.x;
+  const int64_t row = qt * kFwdRows + tid;
+  const bool active = row < p.S_q;
+  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
+  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
+  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
+
+  float qr[DM], acc[DM];
+#pragma unroll
+  for (int d = 0; d < DM; ++d) {
+    qr[d] = (active && d < p.D_qk) ? to_f<T>(Q[row * p.D_qk + d]) * p.scale_log2 : 0.0f;
+    acc[d] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + row) * static_cast<uint64_t>(p.S_kv);
+  int64_t kv_end = p.S_kv;
+  if (p.causal) kv_end = min(p.S_kv, (qt + 1) * kFwdRows);
+  for (int64_t kv0 = 0; kv0 < kv_end; kv0 += kFwdKeys) {
+    __syncthreads();
+    stage_rows<T>(Ks, K, kv0, p.S_kv, kFwdKeys, p.D_qk, DM, tid, kFwdRows);
+    stage_rows<T>(Vs, V, kv0, p.S_kv, kFwdKeys, p.D_v, DM, tid, kFwdRows);
+    __syncthreads();
+    if (!active) continue;
+    float sc[kFwdKeys];
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int jj = 0; jj < kFwdKeys; ++jj) {
+      const int64_t j = kv0 + jj;
+      const bool valid = j < p.S_kv && (!p.causal || j <= row);
+      float s = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) s = fmaf(qr[d], Ks[jj * DM + d], s);
+      sc[jj] = valid ? s : -INFINITY;
+      tmax = fmaxf(tmax, sc[jj]);
+    }
+    if (tmax == -INFINITY) continue;
+    const float m_new = fmaxf(m, tmax);
+    const float alpha = ex2(m - m_new);
+    m = m_new;
+    l *= alpha;
+#pragma unroll
+    for (int d = 0; d < DM; ++d) acc[d] *= alpha;
+#pragma unroll
+    for (int jj = 0; jj < kFwdKeys; ++jj) {
+      float pr = ex2(sc[jj] - m);
+      l += pr;
+      if (p.dropout_on && dropped(lcg_state(rbase, static_cast<uint64_t>(kv0 + jj)), p.drop_thr)) pr = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) acc[d] = fmaf(pr, Vs[jj * DM + d], acc[d]);
+    }
+  }
+  if (!active) return;
+  const int64_t orow = b * p.S_q + row;
+  const float lse = (m == -INFINITY) ? kNegInit + logf(kEps) : m * kLn2 + logf(l + kEps);
+  p.stats[orow] = lse;
+  const float inv = (l > kEps) ? p.dp_inv / l : 0.0f;
+  T* O = static_cast<T*>(p.out) + orow * p.D_v;
+#pragma unroll
+  for (int d = 0; d < DM; ++d)
+    if (d < p.D_v) O[d] = from_f<T>(acc[d] * inv);
+}
+
+// D_i = sum_d dO[i,d] * O[i,d] (fp32), one warp per row.
+template <typename T>
+__global__ void __launch_bounds__(256) delta_kernel(Params p) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= p.B * p.S_q) return;
+  const T* dO = static_cast<const T*>(p.d_o) + row * p.D_v;
+  const T* O = static_cast<const T*>(p.o) + row * p.D_v;
+  float s = 0.0f;
+  for (int d = lane; d < p.D_v; d += 32) s = fmaf(to_f<T>(dO[d]), to_f<T>(O[d]), s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) p.delta[row] = s;
+}
+
+// Gradient of one score element.  Returns false when skipped (p <= 1e-6,
+// sdpa/sdpa_bwd.cu.cc:131); otherwise the dropped-out probability and dS
+// (sdpa/sdpa_bwd.cu.cc:133-157).
+__device__ __forceinline__ bool elem_grad(const Params& p, float s_log2, float lse2, float delta, uint64_t state,
+                                          float dPdot, float& prob, float& dS) {
+  float pr = ex2(s_log2 - lse2);
+  if (!(pr > kEps)) return false;
+  if (p.dropout_on) {
+    if (dropped(state, p.drop_thr)) {
+      dS = p.scale * (-pr * delta);
+      prob = 0.0f;
+      return true;
+    }
+    pr *= p.dp_inv;
+  }
+  dS = p.scale * (pr * (dPdot - delta / p.dp_inv));
+  prob = pr;
+  return true;
+}
+
+template <typename T, int DM>
+__global__ void __launch_bounds__(kBwdRows) dkdv_kernel(Params p) {
+  extern __shared__ float sm[];
+  float* Kt = sm;                         // [DM][kBwdRows]
+  float* Vt = Kt + DM * kBwdRows;         // [DM][kBwdRows]
+  float* Qs = Vt + DM * kBwdRows;         // [kBwdTile][DM]
+  float* dOs = Qs + kBwdTile * DM;        // [kBwdTile][DM]
+  float* lse_s = dOs + kBwdTile * DM;     // [kBwdTile] (log2 units)
+  float* del_s = lse_s + kBwdTile;        // [kBwdTile]
+  const int64_t n_kt = (p.S_kv + kBwdRows - 1) / kBwdRows;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t kt = blockIdx.x / p.B;
+  const int tid = threadIdx.x;
+  const int64_t kv = kt * kBwdRows + tid;
+  const bool active = kv < p.S_kv;
+  (void)n_kt;
+  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
+  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
+  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
+  const T* dO = static_cast<const T*>(p.d_o) + b * p.S_q * p.D_v;
+  for (int d = 0; d < DM; ++d) {
+    Kt[d * kBwdRows + tid] = (active && d < p.D_qk) ? to_f<T>(K[kv * p.D_qk + d]) : 0.0f;
+    Vt[d * kBwdRows + tid] = (active && d < p.D_v) ? to_f<T>(V[kv * p.D_v + d]) : 0.0f;
+  }
+  float dk[DM], dv[DM];
+#pragma unroll
+  for (int d = 0; d < DM; ++d) dk[d] = dv[d] = 0.0f;
+  const int64_t q_start = p.causal ? (kt * kBwdRows / kBwdTile) * kBwdTile : 0;
+  for (int64_t q0 = q_start; q0 < p.S_q; q0 += kBwdTile) {
+    __syncthreads();
+    stage_rows<T>(Qs, Q, q0, p.S_q, kBwdTile, p.D_qk, DM, tid, kBwdRows);
+    stage_rows<T>(dOs, dO, q0, p.S_q, kBwdTile, p.D_v, DM, tid, kBwdRows);
+    for (int r = tid; r < kBwdTile; r += kBwdRows) {
+      const int64_t i = q0 + r;
+      lse_s[r] = i < p.S_q ? p.lse[b * p.S_q + i] * kLog2e : 0.0f;
+      del_s[r] = i < p.S_q ? p.delta[b * p.S_q + i] : 0.0f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    for (int r = 0; r < kBwdTile; ++r) {
+      const int64_t i = q0 + r;
+      if (i >= p.S_q) break;
+      if (p.causal && i < kv) continue;
+      float s = 0.0f, dP = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) s = fmaf(Qs[r * DM + d], Kt[d * kBwdRows + tid], s);
+#pragma unroll
+      for (int d = 0; d < DM; ++d) dP = fmaf(dOs[r * DM + d], Vt[d * kBwdRows + tid], dP);
+      const uint64_t st =
+          lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv),
+                    static_cast<uint64_t>(kv));
+      float pr, dS;
+      if (!elem_grad(p, s * p.scale_log2, lse_s[r], del_s[r], st, dP, pr, dS)) continue;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) {
+        dv[d] = fmaf(pr, dOs[r * DM + d], dv[d]);
+        dk[d] = fmaf(dS, Qs[r * DM + d], dk[d]);
+      }
+    }
+  }
+  if (!active) return;
+  T* dK = static_cast<T*>(p.dk) + (b * p.S_kv + kv) * p.D_qk;
+  T* dV = static_cast<T*>(p.dv) + (b * p.S_kv + kv) * p.D_v;
+#pragma unroll
+  for (int d = 0; d < DM; ++d) {
+    if (d < p.D_qk) dK[d] = from_f<T>(dk[d]);
+    if (d < p.D_v) dV[d] = from_f<T>(dv[d]);
+  }
+}
+
+template <typename T, int DM>
+__global__ void __launch_bounds__(kBwdRows) dq_kernel(Params p) {
+  extern __shared__ float sm[];
+  float* Qt = sm;                     // [DM][kBwdRows]
+  float* dOt = Qt + DM * kBwdRows;    // [DM][kBwdRows]
+  float* Ks = dOt + DM * kBwdRows;    // [kBwdTile][DM]
+  float* Vs = Ks + kBwdTile * DM;     // [kBwdTile][DM]
+  const int64_t n_qt = (p.S_q + kBwdRows - 1) / kBwdRows;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;
+  const int tid = threadIdx.x;
+  const int64_t row = qt * kBwdRows + tid;
+  const bool active = row < p.S_q;
+  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
+  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
+  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
+  const T* dO = static_cast<const T*>(p.d_o) + b * p.S_q * p.D_v;
+  for (int d = 0; d < DM; ++d) {
+    Qt[d * kBwdRows + tid] = (active && d < p.D_qk) ? to_f<T>(Q[row * p.D_qk + d]) : 0.0f;
+    dOt[d * kBwdRows + tid] = (active && d < p.D_v) ? to_f<T>(dO[row * p.D_v + d]) : 0.0f;
+  }
+  const float lse2 = active ? p.lse[b * p.S_q + row] * kLog2e : 0.0f;
+  const float delta = active ? p.delta[b * p.S_q + row] : 0.0f;
+  const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + row) * static_cast<uint64_t>(p.S_kv);
+  float dq[DM];
+#pragma unroll
+  for (int d = 0; d < DM; ++d) dq[d] = 0.0f;
+  int64_t kv_end = p.S_kv;
+  if (p.causal) kv_end = min(p.S_kv, (qt + 1) * kBwdRows);
+  for (int64_t kv0 = 0; kv0 < kv_end; kv0 += kBwdTile) {
+    __syncthreads();
+    stage_rows<T>(Ks, K, kv0, p.S_kv, kBwdTile, p.D_qk, DM, tid, kBwdRows);
+    stage_rows<T>(Vs, V, kv0, p.S_kv, kBwdTile, p.D_v, DM, tid, kBwdRows);
+    __syncthreads();
+    if (!active) continue;
+    for (int jj = 0; jj < kBwdTile; ++jj) {
+      const int64_t j = kv0 + jj;
+      if (j >= p.S_kv) break;
+      if (p.causal && j > row) break;
+      float s = 0.0f, dP = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) s = fmaf(Qt[d * kBwdRows + tid], Ks[jj * DM + d], s);
+#pragma unroll
+      for (int d = 0; d < DM; ++d) dP = fmaf(dOt[d * kBwdRows + tid], Vs[jj * DM + d], dP);
+      float pr, dS;
+      if (!elem_grad(p, s * p.scale_log2, lse2, delta, lcg_state(rbase, static_cast<uint64_t>(j)), dP, pr, dS))
+        continue;
+#pragma unroll
+      for (int d = 0; d < DM; ++d) dq[d] = fmaf(dS, Ks[jj * DM + d], dq[d]);
+    }
+  }
+  if (!active) return;
+  T* dQ = static_cast<T*>(p.dq) + (b * p.S_q + row) * p.D_qk;
+#pragma unroll
+  for (int d = 0; d < DM; ++d)
+    if (d < p.D_qk) dQ[d] = from_f<T>(dq[d]);
+}
+
+template <int DM>
+constexpr size_t dkdv_smem() {
+  return sizeof(float) * (2 * DM * kBwdRows + 2 * kBwdTile * DM + 2 * kBwdTile);
+}
+template <int DM>
+constexpr size_t dq_smem() {
+  return sizeof(float) * (2 * DM * kBwdRows + 2 * kBwdTile * DM);
+}
+
+}  // namespace simt
+}  // namespace sdpa_b200

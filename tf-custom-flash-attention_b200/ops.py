@@ -1,0 +1,177 @@
+"""Host-side mirror of the reference's ``Sdpa`` / ``SdpaGrad`` ops for torch CUDA tensors.
+
+``sdpa`` and ``sdpa_grad`` take the reference ops' inputs and attrs (names,
+meaning, defaults: sdpa/sdpa_ops.cc:7-63), run the reference OpKernels'
+validation with the same messages and order (SdpaFwdOp::Compute
+sdpa/sdpa_cpu.cc:29-87, SdpaBwdOp::Compute sdpa/sdpa_cpu.cc:105-192), allocate
+the outputs like ``allocate_output`` does, and launch the sm_100a kernels
+through the C ABI on the current CUDA stream.
+
+Failed checks raise ``InvalidArgumentError`` (TensorFlow's
+``errors::InvalidArgument``).  Inputs must be CUDA tensors: there is no CPU
+path (the reference's CPU kernels are not part of this library).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+class InvalidArgumentError(ValueError):
+    """Raised where the reference's OP_REQUIRES fails with errors::InvalidArgument."""
+
+
+class KernelError(RuntimeError):
+    """A non-validation failure reported by the C ABI (CUDA error, timeout)."""
+
+
+_DTYPES = {torch.float16: _lib.F16, torch.float32: _lib.F32}
+
+
+def _scalar_u64(x, name: str) -> int:
+    if isinstance(x, torch.Tensor):
+        if x.dim() != 0:
+            raise InvalidArgumentError(f"{name} must be scalar")
+        x = int(x.item())
+    return int(x) & 0xFFFFFFFFFFFFFFFF
+
+
+def _rank3(t: torch.Tensor, idx: int):
+    if t.dim() != 3:
+        raise InvalidArgumentError(f"Shape must be rank 3 but is rank {t.dim()} for input {idx}")
+
+
+def _prep(ts):
+    dt = ts[0].dtype
+    if dt not in _DTYPES:
+        raise InvalidArgumentError(f"T must be half or float, got {dt}")
+    for t in ts:
+        if not t.is_cuda:
+            raise InvalidArgumentError("sdpa_b200 runs on CUDA tensors only (no CPU kernel is registered)")
+        if t.dtype != dt:
+            raise InvalidArgumentError("all floating-point inputs must share dtype T")
+    return [t.contiguous() for t in ts], _DTYPES[dt]
+
+
+def _check(rc: int):
+    if rc == _lib.OK:
+        return
+    if rc in (_lib.EINVAL, _lib.EUNSUPPORTED, _lib.EWORKSPACE):
+        raise InvalidArgumentError(_lib.strerror(rc))
+    raise KernelError(_lib.strerror(rc))
+
+
+_FEATURE_MSG = ("CUDA kernel does not support feature size over 128. Set smaller feature size or use more heads")
+
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seed, offset, scale: float = 1.0, dropout: float = 0.0,
+         causal_mask: bool = False):
+    """The ``Sdpa`` op: returns (output [B,S_q,D_v] T, stats [B,S_q] float32)."""
+    for i, t in enumerate((q, k, v)):
+        _rank3(t, i)
+    seed_v = _scalar_u64(seed, "seed")
+    offset_v = _scalar_u64(offset, "offset")
+    B, S_q, D_qk = q.shape
+    S_kv, D_v = k.shape[1], v.shape[2]
+    if k.shape[0] != B:
+        raise InvalidArgumentError("K batch size mismatch")
+    if k.shape[2] != D_qk:
+        raise InvalidArgumentError("K feature size mismatch")
+    if v.shape[0] != B:
+        raise InvalidArgumentError("V batch size mismatch")
+    if v.shape[1] != S_kv:
+        raise InvalidArgumentError("V seq size mismatch")
+    if causal_mask and S_q != S_kv:
+        raise InvalidArgumentError("seq size Q != K while causal_mask = True")
+    if max(D_qk, D_v) > 128:
+        raise InvalidArgumentError(_FEATURE_MSG)
+    (q, k, v), dt = _prep([q, k, v])
+    out = torch.empty((B, S_q, D_v), dtype=q.dtype, device=q.device)
+    stats = torch.empty((B, S_q), dtype=torch.float32, device=q.device)
+    if B * S_q == 0 or D_v == 0:
+        return out, stats
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream().cuda_stream
+        rc = _lib.lib().sdpa_b200_fwd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                      stats.data_ptr(), B, S_q, S_kv, D_qk, D_v, float(scale), float(dropout),
+                                      int(bool(causal_mask)), seed_v, offset_v, st)
+    _check(rc)
+    return out, stats
+
+
+def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale: float = 1.0,
+              causal_mask: bool = False):
+    """The ``SdpaGrad`` op: returns (dq, dk, dv) shaped like (q, k, v)."""
+    for i, t in enumerate((q, k, v)):
+        _rank3(t, i)
+    seed_v = _scalar_u64(seed, "seed")
+    offset_v = _scalar_u64(offset, "offset")
+    B, S_q, D_qk = q.shape
+    S_kv, D_v = k.shape[1], v.shape[2]
+    checks = [
+        (k.shape[0] == B, "K batch size mismatch"),
+        (k.shape[2] == D_qk, "K feature size mismatch"),
+        (v.shape[0] == B, "V batch size mismatch"),
+        (v.shape[1] == S_kv, "V seq size mismatch"),
+        (out.dim() == 3 and out.shape[0] == B, "O batch size mismatch"),
+        (out.dim() == 3 and out.shape[1] == S_q, "O seq size mismatch"),
+        (out.dim() == 3 and out.shape[2] == D_v, "O feature size mismatch"),
+        (do.dim() == 3 and do.shape[0] == B, "dO batch size mismatch"),
+        (do.dim() == 3 and do.shape[1] == S_q, "dO seq size mismatch"),
+        (do.dim() == 3 and do.shape[2] == D_v, "dO feature size mismatch"),
+        (stats.dim() >= 1 and stats.shape[0] == B, "S batch size mismatch"),
+        (stats.dim() >= 2 and stats.shape[1] == S_q, "S seq size mismatch"),
+        (not causal_mask or S_q == S_kv, "seq size Q != K while causal_mask = True"),
+        (max(D_qk, D_v) <= 128, _FEATURE_MSG),
+    ]
+    for ok, msg in checks:
+        if not ok:
+            raise InvalidArgumentError(msg)
+    (q, k, v, out, do), dt = _prep([q, k, v, out, do])
+    if stats.dtype != torch.float32 or not stats.is_cuda:
+        raise InvalidArgumentError("stats must be a float32 CUDA tensor")
+    stats = stats.contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    L = _lib.lib()
+    ws_bytes = L.sdpa_b200_bwd_workspace_bytes(dt, B, S_q, S_kv, D_qk, D_v)
+    ws = torch.empty((max(ws_bytes, 4) + 3) // 4, dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream().cuda_stream
+        rc = L.sdpa_b200_bwd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), stats.data_ptr(),
+                             do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
+                             float(scale), float(dropout), int(bool(causal_mask)), seed_v, offset_v,
+                             ws.data_ptr(), ws_bytes, st)
+    _check(rc)
+    return dq, dk, dv
+
+
+def dropout_mask(seed, offset, B: int, S_q: int, S_kv: int, dropout: float, device=None) -> torch.Tensor:
+    """uint8 [B,S_q,S_kv], 1 where the kernels drop (b,i,j): the device RNG itself."""
+    m = torch.empty((B, S_q, S_kv), dtype=torch.uint8, device=device or "cuda")
+    if m.numel():
+        st = torch.cuda.current_stream(m.device).cuda_stream
+        _check(_lib.lib().sdpa_b200_dropout_mask(_scalar_u64(seed, "seed"), _scalar_u64(offset, "offset"), B, S_q,
+                                                 S_kv, float(dropout), m.data_ptr(), st))
+    return m
+
+
+def device_status(device=None) -> int:
+    """Reads and clears the device status word (bit 0: a bounded wait timed out)."""
+    w = ctypes.c_uint(0)
+    with torch.cuda.device(device or torch.cuda.current_device()):
+        rc = _lib.lib().sdpa_b200_device_status(ctypes.byref(w), torch.cuda.current_stream().cuda_stream)
+    if rc not in (_lib.OK, _lib.ETIMEOUT):
+        raise KernelError(_lib.strerror(rc))
+    return int(w.value)
+
+
+def kernel_path(dtype: torch.dtype, D_qk: int, D_v: int, backward: bool = False) -> str:
+    """'tcgen05' or 'simt': which kernel family serves this shape."""
+    return "tcgen05" if _lib.lib().sdpa_b200_path(_DTYPES[dtype], D_qk, D_v, int(backward)) else "simt"
+
+
+def last_launch_count() -> int:
+    return int(_lib.lib().sdpa_b200_last_launch_count())
