@@ -15,6 +15,7 @@
 #include "ptx.cuh"
 #include "simt.cuh"
 #include "fwd_tc.cuh"
+#include "bwd_tc.cuh"
 
 using namespace sdpa_b200;
 
@@ -225,6 +226,56 @@ int simt_bwd_dispatch(const Params& p, cudaStream_t st) {
   }
 }
 
+// tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
+template <int DQK, int DV>
+int launch_tc_bwd(const Params& p, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
+  using Cfg = tc::BwdCfg<DQK, DV>;
+  auto kkv = tc::dkdv_kernel<DQK, DV>;
+  auto kq = tc::dq_kernel<DQK, DV>;
+  if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
+  if (ensure_smem(kq, Cfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
+  CUtensorMap k128, v128, q64, do64, q128, do128, k64, v64;
+  if (!make_map_f16(&k128, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&v128, p.v, p.B, p.S_kv, p.D_v, tc::kBwdRows) ||
+      !make_map_f16(&q64, p.q, p.B, p.S_q, p.D_qk, tc::kBwdTile) ||
+      !make_map_f16(&do64, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdTile) ||
+      !make_map_f16(&q128, p.q, p.B, p.S_q, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows) ||
+      !make_map_f16(&k64, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdTile) ||
+      !make_map_f16(&v64, p.v, p.B, p.S_kv, p.D_v, tc::kBwdTile))
+    return SDPA_B200_ECUDA;
+  const int64_t rows = p.B * p.S_q;
+  simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
+  ++t_launches;
+  if (int r = launch_result()) return r;
+  const int64_t gkv = ((p.S_kv + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
+  const int64_t gq = ((p.S_q + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
+  if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kkv<<<static_cast<unsigned>(gkv), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
+  ++t_launches;
+  if (int r = launch_result()) return r;
+  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(q128, do128, k64, v64, p);
+  ++t_launches;
+  return launch_result();
+}
+
+int tc_bwd_dispatch(const Params& p, cudaStream_t st) {
+  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
+  if (q128 && v128) return launch_tc_bwd<128, 128>(p, st);
+  if (q128) return launch_tc_bwd<128, 64>(p, st);
+  if (v128) return launch_tc_bwd<64, 128>(p, st);
+  return launch_tc_bwd<64, 64>(p, st);
+}
+
+bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n) {
+  if (force_simt() || dtype != SDPA_B200_F16 || S_q == 0 || S_kv == 0) return false;
+  if (D_qk % 8 != 0 || D_v % 8 != 0) return false;
+  for (int i = 0; i < n; ++i)
+    if (!aligned16(ptrs[i])) return false;
+  return true;
+}
+
 // --------------------------------------------------------- diagnostics
 __global__ void dropout_mask_kernel(Params p, uint8_t* mask) {
   const int64_t n = p.B * p.S_q * p.S_kv;
@@ -305,6 +356,8 @@ int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const 
   p.dv = dv;
   p.delta = static_cast<float*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
+  if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return tc_bwd_dispatch(p, st);
   return dtype == SDPA_B200_F16 ? simt_bwd_dispatch<__half>(p, st) : simt_bwd_dispatch<float>(p, st);
 }
 
@@ -353,7 +406,7 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
-  if (backward) return 0;
+  (void)backward;
   if (force_simt() || dtype != SDPA_B200_F16) return 0;
   return (D_qk % 8 == 0 && D_v % 8 == 0) ? 1 : 0;
 }

@@ -1,0 +1,492 @@
+// Backward attention on the 5th-generation tensor cores (sm_100a), fp16 in,
+// fp32 accumulate.  Two kernels, as the reference splits it (sdpa/sdpa_bwd.cu.cc:
+// a dK/dV pass over key tiles and a dQ pass over query tiles, no atomics):
+//
+// dkdv_kernel: one CTA = 128 key rows (TMEM lanes) of one batch row; streams
+//   64-row tiles of Q and dO (3-stage TMA ring) and per tile computes
+//     S^T  = K Q^T,  dP^T = V dO^T              (SS MMA, M=128, N=64)
+//     P^T  = exp2(S^T*scale*log2e - lse*log2e), dropout, skip p <= 1e-6
+//     dS^T = P~ (dP^T - D/dp_inv)  or  -p D when dropped   (unscaled)
+//     dV  += P~^T dO,  dK += dS^T Q             (TS MMA: A = P~ / dS read
+//                                                from TMEM, written over S^T / dP^T)
+//   dK is multiplied by `scale` in the epilogue.
+// dq_kernel: one CTA = 128 query rows; streams 64-row K/V tiles; S = Q K^T,
+//   dP = dO V^T, dS as above, dQ += dS K (TS MMA); dQ *= scale at the end.
+//
+// Roles (320 threads): warps 0-7 elementwise (warp w serves TMEM lanes
+// 32*(w%4).. and column half w/4 of each 64-column tile), warp 8 TMA
+// producer, warp 9 MMA issuer + TMEM owner.  S / dP are double-buffered in
+// TMEM so the MMAs of tile j+1 overlap the elementwise work of tile j.
+//
+// Semantics: sdpa/sdpa_bwd.cu.cc:125-170 (dS formulas, skip rule, dropout).
+#pragma once
+#include "common.cuh"
+#include "fwd_tc.cuh"
+#include "ptx.cuh"
+
+namespace sdpa_b200 {
+namespace tc {
+
+constexpr int kBwdThreads = 320;
+constexpr int kBwdRows = 128;   // rows owned by a CTA (TMEM lanes)
+constexpr int kBwdTile = 64;    // rows of each streamed tile
+constexpr int kBwdStages = 3;
+
+template <int DQK, int DV>
+struct BwdCfg {
+  // resident operand (128 rows) and streamed operands (64 rows per stage)
+  static constexpr uint32_t kResA = kBwdRows * DQK * 2;  // K (dkdv) or Q (dq)
+  static constexpr uint32_t kResB = kBwdRows * DV * 2;   // V (dkdv) or dO (dq)
+  static constexpr uint32_t kStA = kBwdTile * DQK * 2;   // Q (dkdv) or K (dq)
+  static constexpr uint32_t kStB = kBwdTile * DV * 2;    // dO (dkdv) or V (dq)
+  static constexpr uint32_t kResAOff = 0;
+  static constexpr uint32_t kResBOff = kResAOff + kResA;
+  static constexpr uint32_t kStAOff = kResBOff + kResB;
+  static constexpr uint32_t kStBOff = kStAOff + kBwdStages * kStA;
+  static constexpr uint32_t kVecOff = kStBOff + kBwdStages * kStB;  // per-tile row vectors
+  static constexpr uint32_t kVecBytes = 2 * 3 * kBwdTile * 4;       // 2 buffers x {lse2, delta, delta/dp_inv}
+  static constexpr uint32_t kBarOff = kVecOff + kVecBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM columns
+  static constexpr uint32_t kAcc0 = 0;     // dV (dkdv) or dQ (dq)
+  static constexpr uint32_t kAcc1 = DV;    // dK (dkdv)
+  static constexpr uint32_t kS = 256;      // S / S^T buffers: 256 + sb*64
+  static constexpr uint32_t kDP = 384;     // dP / dP^T buffers: 384 + sb*64
+  static_assert(DQK + DV <= 256, "TMEM budget");
+};
+
+struct BwdBarriers {
+  uint64_t res_full;
+  uint64_t st_full[kBwdStages];
+  uint64_t st_empty[kBwdStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t vec_ready[2];
+  uint64_t acc_done;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Elementwise gradient of one score: inputs s (raw dot product), dP, the
+// row terms; outputs the dropped-out probability (for dV) and the unscaled dS.
+struct GradTerms {
+  float scale_log2, dp_inv;
+  uint64_t thr;
+  int dropout_on;
+};
+__device__ __forceinline__ void grad_elem(const GradTerms& g, bool valid, float s, float dp, float lse2, float delta,
+                                          float delta_k, uint64_t state, float& pt, float& ds) {
+  float p = ex2(fmaf(s, g.scale_log2, -lse2));
+  if (!valid || !(p > kEps)) {  // masked, or skipped as in sdpa/sdpa_bwd.cu.cc:131
+    pt = 0.0f;
+    ds = 0.0f;
+    return;
+  }
+  if (g.dropout_on && dropped(state, g.thr)) {
+    pt = 0.0f;
+    ds = -p * delta;
+    return;
+  }
+  pt = p * g.dp_inv;
+  ds = pt * (dp - delta_k);
+}
+
+// Shared prologue of both backward kernels: barriers, TMEM, wait control.
+__device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols, int warp) {
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->res_full, 1);
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(&bars->st_full[s], 1);
+      mbar_init(&bars->st_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->p_full[s], 256);
+      mbar_init(&bars->vec_ready[s], 256);
+    }
+    mbar_init(&bars->acc_done, 1);
+    mbar_init(&bars->mma_done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) tmem_alloc(&bars->tmem_base, tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// Producer of both kernels: the resident 128-row pair once, then n 64-row
+// tiles (rows tile0*64 ..) of the streamed pair through the stage ring.
+template <int DA, int DB, typename Cfg>
+__device__ __forceinline__ void bwd_producer(uint8_t* smem, BwdBarriers* bars, const CUtensorMap* ra,
+                                             const CUtensorMap* rb, const CUtensorMap* sa, const CUtensorMap* sb,
+                                             int res_row0, int tile0, int n, int b, const WaitCtl& ctl,
+                                             uint64_t timeout_ns) {
+  mbar_expect_tx(&bars->res_full, Cfg::kResA + Cfg::kResB);
+#pragma unroll
+  for (int c = 0; c < DA / 64; ++c)
+    tma_load_3d(smem + Cfg::kResAOff + c * kBwdRows * 128, ra, c * 64, res_row0, b, &bars->res_full);
+#pragma unroll
+  for (int c = 0; c < DB / 64; ++c)
+    tma_load_3d(smem + Cfg::kResBOff + c * kBwdRows * 128, rb, c * 64, res_row0, b, &bars->res_full);
+  int issued = 0;
+  for (int t = 0; t < n; ++t) {
+    const int s = t % kBwdStages;
+    if (!mbar_wait(&bars->st_empty[s], ((t / kBwdStages) & 1) ^ 1, ctl)) break;
+    const int row0 = (tile0 + t) * kBwdTile;
+    mbar_expect_tx(&bars->st_full[s], Cfg::kStA + Cfg::kStB);
+#pragma unroll
+    for (int c = 0; c < DA / 64; ++c)
+      tma_load_3d(smem + Cfg::kStAOff + s * Cfg::kStA + c * kBwdTile * 128, sa, c * 64, row0, b, &bars->st_full[s]);
+#pragma unroll
+    for (int c = 0; c < DB / 64; ++c)
+      tma_load_3d(smem + Cfg::kStBOff + s * Cfg::kStB + c * kBwdTile * 128, sb, c * 64, row0, b, &bars->st_full[s]);
+    issued = t + 1;
+  }
+  if (*ctl.abort_flag) {  // let copies in flight land before the CTA exits
+    WaitCtl drain = ctl;
+    drain.deadline_ns = globaltimer_ns() + timeout_ns;
+    int dummy = 0;
+    drain.abort_flag = &dummy;
+    mbar_wait(&bars->res_full, 0, drain);
+    for (int t = (issued > kBwdStages ? issued - kBwdStages : 0); t < issued; ++t)
+      mbar_wait(&bars->st_full[t % kBwdStages], (t / kBwdStages) & 1, drain);
+  }
+}
+
+// 128 x 64 score tiles of both kernels: X[sb] = resA * stA^T (K = DA) and
+// Y[sb] = resB * stB^T (K = DB), both operands K-major.
+template <int DA, int DB, typename Cfg>
+__device__ __forceinline__ void bwd_issue_scores(uint32_t tmem, uint32_t smem_base, int s, int sb) {
+  constexpr uint32_t idesc = make_idesc(kBwdRows, kBwdTile, false, false, false);
+  const uint32_t ra = smem_base + Cfg::kResAOff, rb = smem_base + Cfg::kResBOff;
+  const uint32_t sa = smem_base + Cfg::kStAOff + s * Cfg::kStA, sbb = smem_base + Cfg::kStBOff + s * Cfg::kStB;
+#pragma unroll
+  for (int kk = 0; kk < DA / 16; ++kk) {
+    const uint64_t a = make_sw128_desc(ra + (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32, 16, 1024);
+    const uint64_t bb = make_sw128_desc(sa + (kk >> 2) * (kBwdTile * 128) + (kk & 3) * 32, 16, 1024);
+    mma_f16_ss(tmem + Cfg::kS + sb * kBwdTile, a, bb, idesc, kk > 0 ? 1u : 0u);
+  }
+#pragma unroll
+  for (int kk = 0; kk < DB / 16; ++kk) {
+    const uint64_t a = make_sw128_desc(rb + (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32, 16, 1024);
+    const uint64_t bb = make_sw128_desc(sbb + (kk >> 2) * (kBwdTile * 128) + (kk & 3) * 32, 16, 1024);
+    mma_f16_ss(tmem + Cfg::kDP + sb * kBwdTile, a, bb, idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// acc (+)= A[tmem: fp16 pairs over buffer `a_col`, 64 K-elements in two
+// 16-column runs at +0 and +32] * B[64-row stage tile, MN-major, N = DN].
+template <int DN>
+__device__ __forceinline__ void bwd_issue_acc(uint32_t acc_tmem, uint32_t a_col, uint32_t b_tile, bool first) {
+  constexpr uint32_t idesc = make_idesc(kBwdRows, DN, false, true, false);
+#pragma unroll
+  for (int kk = 0; kk < kBwdTile / 16; ++kk) {
+    const uint64_t bd = make_sw128_desc(b_tile + kk * 16 * 128, kBwdTile * 128, 1024);
+    mma_f16_ts(acc_tmem, a_col + (kk >> 1) * 32 + (kk & 1) * 8, bd, idesc, (!first || kk > 0) ? 1u : 0u);
+  }
+}
+
+// Epilogue: TMEM accumulator columns [col0, col0 + 32*nchunks) of this
+// thread's lane, times `mul`, to fp16 row `dst` (columns < D valid).
+__device__ __forceinline__ void store_acc_row(uint32_t taddr, int nchunks, int col0, float mul, bool have_acc,
+                                              bool active, __half* dst, int D) {
+  for (int c = 0; c < nchunks; ++c) {
+    uint32_t o[32];
+    if (have_acc) {
+      SDPA_TMEM_LD32(taddr + c * 32, o);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = 0u;
+    }
+    uint32_t h[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) h[e] = pack_half2(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
+    if (active) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int col = col0 + c * 32 + w * 8;
+        if (col < D) *reinterpret_cast<uint4*>(dst + col) = make_uint4(h[4 * w], h[4 * w + 1], h[4 * w + 2], h[4 * w + 3]);
+      }
+    }
+  }
+}
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do, const Params p) {
+  using Cfg = BwdCfg<DQK, DV>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + Cfg::kBarOff);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t kt = blockIdx.x / p.B;  // low key tiles see the most causal rows: issued first
+  const int64_t n0 = kt * kBwdRows;
+  const int n_qtiles = static_cast<int>((p.S_q + kBwdTile - 1) / kBwdTile);
+  const int tile0 = p.causal ? static_cast<int>(n0 / kBwdTile) : 0;
+  const int nq = n_qtiles - tile0 > 0 ? n_qtiles - tile0 : 0;
+
+  bwd_setup(bars, Cfg::kTmemCols, warp);
+  const uint32_t tmem = bars->tmem_base;
+  WaitCtl ctl;
+  ctl.deadline_ns = globaltimer_ns() + p.timeout_ns;
+  ctl.abort_flag = &bars->abort_flag;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 8) {
+    if (lane == 0 && nq > 0)
+      bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_k, &tm_v, &tm_q, &tm_do, static_cast<int>(n0), tile0, nq,
+                                 static_cast<int>(b), ctl, p.timeout_ns);
+  } else if (warp == 9) {
+    if (lane == 0 && nq > 0) {
+      bool ok = mbar_wait(&bars->res_full, 0, ctl);
+      auto grads = [&](int t) -> bool {
+        const int s = t % kBwdStages, sb = t & 1;
+        if (!mbar_wait(&bars->p_full[sb], (t >> 1) & 1, ctl)) return false;
+        tc_fence_after();
+        // dV += P~^T dO_t ; dK += dS^T Q_t
+        bwd_issue_acc<DV>(tmem + Cfg::kAcc0, tmem + Cfg::kS + sb * kBwdTile, sbase + Cfg::kStBOff + s * Cfg::kStB,
+                          t == 0);
+        bwd_issue_acc<DQK>(tmem + Cfg::kAcc1, tmem + Cfg::kDP + sb * kBwdTile, sbase + Cfg::kStAOff + s * Cfg::kStA,
+                           t == 0);
+        mma_commit(&bars->st_empty[s]);
+        return true;
+      };
+      for (int t = 0; ok && t < nq; ++t) {
+        const int s = t % kBwdStages, sb = t & 1;
+        if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S^T = K Q^T, dP^T = V dO^T
+        mma_commit(&bars->s_full[sb]);
+        if (t > 0 && !grads(t - 1)) ok = false;
+      }
+      if (ok) ok = grads(nq - 1);
+      mma_commit(&bars->acc_done);
+      mma_commit(&bars->mma_done);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else {
+    // ------------------------------------------------ elementwise warps
+    const int e = threadIdx.x;                // 0..255
+    const int half = warp >> 2;               // column half of each 64-wide tile
+    const int r = (warp & 3) * 32 + lane;     // TMEM lane = key row in tile
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int col0 = half * 32;
+    const int64_t j = n0 + r;                 // key row
+    float* vec = reinterpret_cast<float*>(smem + Cfg::kVecOff);  // [2][3][64]
+    GradTerms g;
+    g.scale_log2 = p.scale_log2;
+    g.dp_inv = p.dp_inv;
+    g.thr = p.drop_thr;
+    g.dropout_on = p.dropout_on;
+    const uint64_t step_i = static_cast<uint64_t>(p.S_kv) * kLcgA;  // counter step between query rows
+    auto row_val = [&](int t) -> float {      // this thread's share of tile t's row vectors
+      const int64_t i = static_cast<int64_t>(tile0 + t) * kBwdTile + (e & 63);
+      const int which = e >> 6;
+      if (which >= 3) return 0.0f;
+      if (i >= p.S_q) return which == 0 ? INFINITY : 0.0f;
+      if (which == 0) return p.lse[b * p.S_q + i] * kLog2e;
+      const float d = p.delta[b * p.S_q + i];
+      return which == 1 ? d : d / p.dp_inv;
+    };
+    float pre = nq > 0 ? row_val(0) : 0.0f;
+    bool ok = true;
+    for (int t = 0; t < nq; ++t) {
+      const int sb = t & 1;
+      float* vb = vec + sb * 3 * kBwdTile;
+      if (e < 3 * kBwdTile) vb[e] = pre;
+      mbar_arrive(&bars->vec_ready[sb]);
+      if (t + 1 < nq) pre = row_val(t + 1);
+      if (!warp_wait(&bars->vec_ready[sb], (t >> 1) & 1, ctl) || !warp_wait(&bars->s_full[sb], (t >> 1) & 1, ctl)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dpv[32];
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, sv);
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dpv);
+      tmem_wait_ld();
+      const int64_t i0 = static_cast<int64_t>(tile0 + t) * kBwdTile + col0;
+      uint64_t st = lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i0) * static_cast<uint64_t>(p.S_kv),
+                              static_cast<uint64_t>(j));
+      uint32_t pk[16], dk[16];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        float pt0, ds0, pt1, ds1;
+        grad_elem(g, !p.causal || i0 + c >= j, __uint_as_float(sv[c]), __uint_as_float(dpv[c]), vb[col0 + c],
+                  vb[kBwdTile + col0 + c], vb[2 * kBwdTile + col0 + c], st, pt0, ds0);
+        st += step_i;
+        grad_elem(g, !p.causal || i0 + c + 1 >= j, __uint_as_float(sv[c + 1]), __uint_as_float(dpv[c + 1]),
+                  vb[col0 + c + 1], vb[kBwdTile + col0 + c + 1], vb[2 * kBwdTile + col0 + c + 1], st, pt1, ds1);
+        st += step_i;
+        pk[c / 2] = pack_half2(pt0, pt1);
+        dk[c / 2] = pack_half2(ds0, ds1);
+      }
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, pk);
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[sb]);
+    }
+    if (ok && nq > 0) ok = warp_wait(&bars->acc_done, 0, ctl);
+    if (ok) {
+      tc_fence_after();
+      const bool active = j < p.S_kv;
+      __half* dv_row = static_cast<__half*>(p.dv) + (b * p.S_kv + j) * p.D_v;
+      __half* dk_row = static_cast<__half*>(p.dk) + (b * p.S_kv + j) * p.D_qk;
+      store_acc_row(tmem + lane_base + Cfg::kAcc0 + half * (DV / 2), DV / 64, half * (DV / 2), 1.0f, nq > 0, active,
+                    dv_row, p.D_v);
+      store_acc_row(tmem + lane_base + Cfg::kAcc1 + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nq > 0,
+                    active, dk_row, p.D_qk);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+              const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using Cfg = BwdCfg<DQK, DV>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + Cfg::kBarOff);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int64_t n_qt = (p.S_q + kBwdRows - 1) / kBwdRows;
+  const int64_t b = blockIdx.x % p.B;
+  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
+  const int64_t m0 = qt * kBwdRows;
+  const int64_t n_kv_all = (p.S_kv + kBwdTile - 1) / kBwdTile;
+  const int nkv = static_cast<int>(p.causal ? min(n_kv_all, (m0 + kBwdRows - 1) / kBwdTile + 1) : n_kv_all);
+
+  bwd_setup(bars, Cfg::kTmemCols, warp);
+  const uint32_t tmem = bars->tmem_base;
+  WaitCtl ctl;
+  ctl.deadline_ns = globaltimer_ns() + p.timeout_ns;
+  ctl.abort_flag = &bars->abort_flag;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 8) {
+    if (lane == 0 && nkv > 0)
+      bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_q, &tm_do, &tm_k, &tm_v, static_cast<int>(m0), 0, nkv,
+                                 static_cast<int>(b), ctl, p.timeout_ns);
+  } else if (warp == 9) {
+    if (lane == 0 && nkv > 0) {
+      bool ok = mbar_wait(&bars->res_full, 0, ctl);
+      auto grads = [&](int t) -> bool {
+        const int s = t % kBwdStages, sb = t & 1;
+        if (!mbar_wait(&bars->p_full[sb], (t >> 1) & 1, ctl)) return false;
+        tc_fence_after();
+        // dQ += dS K_t
+        bwd_issue_acc<DQK>(tmem + Cfg::kAcc0, tmem + Cfg::kDP + sb * kBwdTile, sbase + Cfg::kStAOff + s * Cfg::kStA,
+                           t == 0);
+        mma_commit(&bars->st_empty[s]);
+        return true;
+      };
+      for (int t = 0; ok && t < nkv; ++t) {
+        const int s = t % kBwdStages, sb = t & 1;
+        if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S = Q K^T, dP = dO V^T
+        mma_commit(&bars->s_full[sb]);
+        if (t > 0 && !grads(t - 1)) ok = false;
+      }
+      if (ok) ok = grads(nkv - 1);
+      mma_commit(&bars->acc_done);
+      mma_commit(&bars->mma_done);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else {
+    // ------------------------------------------------ elementwise warps
+    const int half = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // TMEM lane = query row in tile
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int col0 = half * 32;
+    const int64_t i = m0 + r;
+    const bool row_ok = i < p.S_q;
+    const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
+    const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
+    const float delta_k = delta / p.dp_inv;
+    GradTerms g;
+    g.scale_log2 = p.scale_log2;
+    g.dp_inv = p.dp_inv;
+    g.thr = p.drop_thr;
+    g.dropout_on = p.dropout_on;
+    const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv);
+    bool ok = true;
+    for (int t = 0; t < nkv; ++t) {
+      const int sb = t & 1;
+      if (!warp_wait(&bars->s_full[sb], (t >> 1) & 1, ctl)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dpv[32];
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, sv);
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dpv);
+      tmem_wait_ld();
+      const int64_t j0 = static_cast<int64_t>(t) * kBwdTile + col0;
+      int64_t lim64 = p.S_kv - j0;
+      if (p.causal) lim64 = min(lim64, i - j0 + 1);
+      const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
+      uint64_t st = lcg_state(rbase, static_cast<uint64_t>(j0));
+      uint32_t dk[16];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        float pt0, ds0, pt1, ds1;
+        grad_elem(g, c < lim, __uint_as_float(sv[c]), __uint_as_float(dpv[c]), lse2, delta, delta_k, st, pt0, ds0);
+        st += kLcgA;
+        grad_elem(g, c + 1 < lim, __uint_as_float(sv[c + 1]), __uint_as_float(dpv[c + 1]), lse2, delta, delta_k, st,
+                  pt1, ds1);
+        st += kLcgA;
+        dk[c / 2] = pack_half2(ds0, ds1);
+      }
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[sb]);
+    }
+    if (ok && nkv > 0) ok = warp_wait(&bars->acc_done, 0, ctl);
+    if (ok) {
+      tc_fence_after();
+      __half* dq_row = static_cast<__half*>(p.dq) + (b * p.S_q + i) * p.D_qk;
+      store_acc_row(tmem + lane_base + Cfg::kAcc0 + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nkv > 0,
+                    row_ok, dq_row, p.D_qk);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace tc
+}  // namespace sdpa_b200
