@@ -133,8 +133,10 @@ int launch_result() {
   return e == cudaSuccess ? SDPA_B200_OK : SDPA_B200_ECUDA;
 }
 
-bool tc_fwd_ok(int dtype, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v, const void* o) {
+bool tc_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
+               const void* o) {
   if (force_simt() || dtype != SDPA_B200_F16) return false;
+  if (S_kv == 0) return false;  // a TMA map cannot have a zero extent
   if (D_qk % 8 != 0 || D_v % 8 != 0) return false;  // TMA row strides must be 16-byte multiples
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
 }
@@ -323,7 +325,7 @@ int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* 
   p.out = out;
   p.stats = stats;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (tc_fwd_ok(dtype, D_qk, D_v, q, k, v, out)) return tc_fwd_dispatch(p, st);
+  if (tc_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return tc_fwd_dispatch(p, st);
   return dtype == SDPA_B200_F16 ? simt_fwd_dispatch<__half>(p, st) : simt_fwd_dispatch<float>(p, st);
 }
 
