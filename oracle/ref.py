@@ -119,7 +119,7 @@ def _run(op, device, tensors, seed, offset, outs, scale, dropout, causal):
     c_odims = (ctypes.c_long * (3 * n_out))()
     err = ctypes.create_string_buffer(512)
     stream = None
-    if device == "GPU":
+    if device == "GPU" and not isinstance(tensors[0], np.ndarray):
         import torch  # noqa: PLC0415
 
         stream = torch.cuda.current_stream().cuda_stream

@@ -98,6 +98,7 @@ int ref_run(const char* op, const char* device, int dtype, int n_in, void** in_p
   ctx.output_buffers.assign(out_ptrs, out_ptrs + n_out);
   ctx.outputs.resize(n_out);  // allocate_output hands out pointers into this vector
   ctx.gpu_device.stream_ = stream;
+  ctx.gpu_temp = std::string(device) == "GPU";
   {
     std::lock_guard<std::mutex> lk(g_err_mu);
     g_launch_err.clear();

@@ -23,6 +23,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <cstdio>
 #include <cmath>
@@ -301,6 +302,21 @@ class Tensor {
     return m;
   }
   void* raw() const { return ptr_; }
+  long NumElements() const { return shape_.num_elements(); }
+  template <typename T>
+  typename TTypes<T, 1>::ConstTensor flat() const {
+    typename TTypes<T, 1>::ConstTensor m;
+    m.ptr = static_cast<const T*>(ptr_);
+    m.dims[0] = shape_.num_elements();
+    return m;
+  }
+  template <typename T>
+  typename TTypes<T, 1>::Tensor flat() {
+    typename TTypes<T, 1>::Tensor m;
+    m.ptr = static_cast<T*>(ptr_);
+    m.dims[0] = shape_.num_elements();
+    return m;
+  }
 
  private:
   void* ptr_ = nullptr;
@@ -336,8 +352,39 @@ class OpKernelConstruction {
   Status status_;
 };
 
+enum DataType { DT_FLOAT = 1, DT_HALF = 19 };
+
 class OpKernelContext {
  public:
+  // Scratch handed out by allocate_temp: device memory when a CUDA runtime is
+  // available and gpu_temp is set (a GPU kernel runs), host memory otherwise.
+  bool gpu_temp = false;
+  std::vector<void*> temps;
+  ~OpKernelContext() {
+    for (void* t : temps) {
+#if defined(TFS_HAVE_CUDA_RT)
+      if (gpu_temp) {
+        cudaFree(t);
+        continue;
+      }
+#endif
+      std::free(t);
+    }
+  }
+  Status allocate_temp(DataType dt, const TensorShape& s, Tensor* out) {
+    size_t bytes = static_cast<size_t>(s.num_elements()) * (dt == DT_HALF ? 2 : 4);
+    if (bytes == 0) bytes = 4;
+    void* p = nullptr;
+#if defined(TFS_HAVE_CUDA_RT)
+    if (gpu_temp) {
+      if (cudaMalloc(&p, bytes) != cudaSuccess) return errors::Internal("allocate_temp failed");
+    } else
+#endif
+      p = std::malloc(bytes);
+    temps.push_back(p);
+    *out = Tensor(p, s);
+    return OkStatus();
+  }
   std::vector<Tensor> inputs;
   std::vector<void*> output_buffers;  // caller-owned memory for each output
   std::vector<Tensor> outputs;
