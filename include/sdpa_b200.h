@@ -45,7 +45,8 @@ enum sdpa_b200_status {
   SDPA_B200_EUNSUPPORTED = 2, /* max(D_qk, D_v) > 128                          */
   SDPA_B200_ECUDA = 3,        /* a CUDA runtime / launch error                 */
   SDPA_B200_ETIMEOUT = 4,     /* a device-side wait gave up (see status word)  */
-  SDPA_B200_EWORKSPACE = 5    /* workspace missing or too small                */
+  SDPA_B200_EWORKSPACE = 5,   /* workspace missing or too small                */
+  SDPA_B200_ESCRATCH = 6      /* problem too large for the built-in scratch    */
 };
 
 /* Forward: out [B,S_q,D_v] (dtype), stats [B,S_q] float32.
@@ -94,6 +95,32 @@ int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward);
 
 /* Number of kernel launches the last successful fwd/bwd call on this thread made. */
 int sdpa_b200_last_launch_count(void);
+
+/* Backward for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same arguments and results as
+ * sdpa_b200_bwd, but without a workspace: the per-row scratch
+ * (rowsum(dO*O), one float per query row) lives in a fixed array of
+ * SDPA_B200_NOALLOC_MAX_ROWS floats (4 MiB) built into the library, which
+ * every GPU that loads the library keeps until the process exits.
+ *   - Meant for hosts such as a framework's memory-planned executor, a
+ *     real-time or embedded runtime, or code running where cudaMalloc is
+ *     forbidden or would stall; nothing here calls cudaMalloc, cudaFree or
+ *     any allocating routine.
+ *   - B * S_q must not exceed SDPA_B200_NOALLOC_MAX_ROWS; larger problems
+ *     return SDPA_B200_ESCRATCH and launch nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents
+ *     (every row used is rewritten before it is read, so nothing needs to
+ *     start at zero).  Calls whose kernels overlap on the GPU -- different
+ *     streams, or different host threads, on the same device -- race on it:
+ *     order them on one stream or serialise them. */
+#define SDPA_B200_NOALLOC_MAX_ROWS (1 << 20)
+int sdpa_b200_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out,
+                          const float* stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B,
+                          int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
+                          int causal, uint64_t seed, uint64_t offset, void* stream);
 
 /* ABI version (major*100 + minor). */
 int sdpa_b200_version(void);

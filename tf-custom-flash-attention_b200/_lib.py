@@ -11,7 +11,8 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsdpa_b200.so")
 
-OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, EWORKSPACE = range(6)
+OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, EWORKSPACE, ESCRATCH = range(7)
+NOALLOC_MAX_ROWS = 1 << 20
 F16, F32 = 0, 1
 
 _lib = None
@@ -33,6 +34,9 @@ def lib() -> ctypes.CDLL:
     L.sdpa_b200_bwd.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32, ci, u64,
                                 u64, vp, sz, vp]
     L.sdpa_b200_bwd.restype = ci
+    L.sdpa_b200_bwd_noalloc.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32,
+                                        ci, u64, u64, vp]
+    L.sdpa_b200_bwd_noalloc.restype = ci
     L.sdpa_b200_dropout_mask.argtypes = [u64, u64, i64, i64, i64, f32, vp, vp]
     L.sdpa_b200_dropout_mask.restype = ci
     L.sdpa_b200_strerror.argtypes = [ci]
@@ -60,4 +64,5 @@ EXPORTS = (
     "sdpa_b200_fwd", "sdpa_b200_bwd_workspace_bytes", "sdpa_b200_bwd", "sdpa_b200_dropout_mask",
     "sdpa_b200_strerror", "sdpa_b200_device_status", "sdpa_b200_set_wait_timeout_ns",
     "sdpa_b200_test_wait_timeout", "sdpa_b200_path", "sdpa_b200_last_launch_count", "sdpa_b200_version",
+    "sdpa_b200_bwd_noalloc",
 )

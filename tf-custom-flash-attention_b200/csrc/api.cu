@@ -385,6 +385,7 @@ const char* sdpa_b200_strerror(int status) {
     case SDPA_B200_ECUDA: return "CUDA error";
     case SDPA_B200_ETIMEOUT: return "a device-side wait timed out";
     case SDPA_B200_EWORKSPACE: return "workspace missing, misaligned or too small";
+    case SDPA_B200_ESCRATCH: return "B * S_q exceeds the built-in scratch of sdpa_b200_bwd_noalloc (1048576 rows)";
     default: return "unknown status";
   }
 }
@@ -416,5 +417,47 @@ int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
 int sdpa_b200_last_launch_count(void) { return t_launches; }
 
 int sdpa_b200_version(void) { return 100; }
+
+}  // extern "C"
+
+// ------------------------------------------------ backward without allocation
+// The per-row scratch of sdpa_b200_bwd_noalloc.  Host code must not pass the
+// symbol itself to a kernel (on the host it only names a stand-in); its device
+// address is looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) float g_noalloc_scratch[SDPA_B200_NOALLOC_MAX_ROWS];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// Device address of the scratch array on the current device (looked up on
+// the first call per device).  Returns nullptr when the lookup fails.
+void* noalloc_scratch_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+extern "C" {
+
+int sdpa_b200_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out,
+                          const float* stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B,
+                          int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
+                          int causal, uint64_t seed, uint64_t offset, void* stream) {
+  t_launches = 0;
+  if (int r = check_common(dtype, B, S_q, S_kv, D_qk, D_v, causal)) return r;
+  if (B * S_q > SDPA_B200_NOALLOC_MAX_ROWS) return SDPA_B200_ESCRATCH;
+  void* scratch = noalloc_scratch_ptr();
+  if (!scratch) return SDPA_B200_ECUDA;
+  return sdpa_b200_bwd(dtype, q, k, v, out, stats, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,
+                       causal, seed, offset, scratch, sizeof(float) * SDPA_B200_NOALLOC_MAX_ROWS, stream);
+}
 
 }  // extern "C"
