@@ -10,14 +10,11 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/sdpa_b200.h"
-#include "common.cuh"
+#include "host.cuh"
 #include "ptx.cuh"
-#include "simt.cuh"
-#include "fwd_tc.cuh"
-#include "bwd_tc.cuh"
 
 using namespace sdpa_b200;
+using namespace sdpa_b200::host;
 
 namespace {
 
@@ -43,14 +40,6 @@ uint64_t drop_threshold(float rate) {
       hi = mid;
   }
   return lo;
-}
-
-int dmax_bucket(int64_t d) {
-  if (d <= 8) return 8;
-  if (d <= 16) return 16;
-  if (d <= 32) return 32;
-  if (d <= 64) return 64;
-  return 128;
 }
 
 Params make_params(int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
@@ -83,191 +72,12 @@ int check_common(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, 
   return SDPA_B200_OK;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-// ---------------------------------------------------------------- TMA maps
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
-// [B, S, D] fp16 tensor, box = 64 columns x `rows` rows x 1 batch, 128B swizzle.
-// Columns beyond D and rows beyond S read as zero.
-bool make_map_f16(CUtensorMap* m, const void* base, int64_t B, int64_t S, int64_t D, int rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(rows), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-// Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
-template <typename K>
-cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done_mask) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done_mask.load() & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess) done_mask.fetch_or(bit);
-  return e;
-}
-
-int launch_result() {
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SDPA_B200_OK : SDPA_B200_ECUDA;
-}
-
 bool tc_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
                const void* o) {
   if (force_simt() || dtype != SDPA_B200_F16) return false;
   if (S_kv == 0) return false;  // a TMA map cannot have a zero extent
   if (D_qk % 8 != 0 || D_v % 8 != 0) return false;  // TMA row strides must be 16-byte multiples
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
-}
-
-// ----------------------------------------------------------------- forward
-template <int DQK, int DV>
-int launch_tc_fwd(const Params& p, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_done{0};
-  using Cfg = tc::FwdCfg<DQK, DV>;
-  auto kern = tc::fwd_kernel<DQK, DV>;
-  if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
-  CUtensorMap mq, mk, mv;
-  if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
-      !make_map_f16(&mv, p.v, p.B, p.S_kv, p.D_v, tc::kBN))
-    return SDPA_B200_ECUDA;
-  const int64_t n_qt = (p.S_q + tc::kBM - 1) / tc::kBM;
-  const int64_t grid = n_qt * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tc::kFwdThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
-  ++t_launches;
-  return launch_result();
-}
-
-template <typename T, int DM>
-int launch_simt_fwd(const Params& p, cudaStream_t st) {
-  const int64_t grid = ((p.S_q + simt::kFwdRows - 1) / simt::kFwdRows) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  simt::fwd_kernel<T, DM><<<static_cast<unsigned>(grid), simt::kFwdRows, 0, st>>>(p);
-  ++t_launches;
-  return launch_result();
-}
-
-template <typename T>
-int simt_fwd_dispatch(const Params& p, cudaStream_t st) {
-  switch (dmax_bucket(p.D_qk > p.D_v ? p.D_qk : p.D_v)) {
-    case 8: return launch_simt_fwd<T, 8>(p, st);
-    case 16: return launch_simt_fwd<T, 16>(p, st);
-    case 32: return launch_simt_fwd<T, 32>(p, st);
-    case 64: return launch_simt_fwd<T, 64>(p, st);
-    default: return launch_simt_fwd<T, 128>(p, st);
-  }
-}
-
-int tc_fwd_dispatch(const Params& p, cudaStream_t st) {
-  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
-  if (q128 && v128) return launch_tc_fwd<128, 128>(p, st);
-  if (q128) return launch_tc_fwd<128, 64>(p, st);
-  if (v128) return launch_tc_fwd<64, 128>(p, st);
-  return launch_tc_fwd<64, 64>(p, st);
-}
-
-// ---------------------------------------------------------------- backward
-template <typename T, int DM>
-int launch_simt_bwd(const Params& p, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
-  const int64_t rows = p.B * p.S_q;
-  if (rows > 0) {
-    simt::delta_kernel<T><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
-    ++t_launches;
-    if (int r = launch_result()) return r;
-  }
-  const size_t smkv = simt::dkdv_smem<DM>(), smq = simt::dq_smem<DM>();
-  if (ensure_smem(simt::dkdv_kernel<T, DM>, smkv, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (ensure_smem(simt::dq_kernel<T, DM>, smq, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
-  const int64_t gkv = ((p.S_kv + simt::kBwdRows - 1) / simt::kBwdRows) * p.B;
-  const int64_t gq = ((p.S_q + simt::kBwdRows - 1) / simt::kBwdRows) * p.B;
-  if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  if (gkv > 0) {
-    simt::dkdv_kernel<T, DM><<<static_cast<unsigned>(gkv), simt::kBwdRows, smkv, st>>>(p);
-    ++t_launches;
-    if (int r = launch_result()) return r;
-  }
-  if (gq > 0) {
-    simt::dq_kernel<T, DM><<<static_cast<unsigned>(gq), simt::kBwdRows, smq, st>>>(p);
-    ++t_launches;
-    if (int r = launch_result()) return r;
-  }
-  return SDPA_B200_OK;
-}
-
-template <typename T>
-int simt_bwd_dispatch(const Params& p, cudaStream_t st) {
-  switch (dmax_bucket(p.D_qk > p.D_v ? p.D_qk : p.D_v)) {
-    case 8: return launch_simt_bwd<T, 8>(p, st);
-    case 16: return launch_simt_bwd<T, 16>(p, st);
-    case 32: return launch_simt_bwd<T, 32>(p, st);
-    case 64: return launch_simt_bwd<T, 64>(p, st);
-    default: return launch_simt_bwd<T, 128>(p, st);
-  }
-}
-
-// tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
-template <int DQK, int DV>
-int launch_tc_bwd(const Params& p, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
-  using Cfg = tc::BwdCfg<DQK, DV>;
-  auto kkv = tc::dkdv_kernel<DQK, DV>;
-  auto kq = tc::dq_kernel<DQK, DV>;
-  if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (ensure_smem(kq, Cfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
-  CUtensorMap k128, v128, q64, do64, q128, do128, k64, v64;
-  if (!make_map_f16(&k128, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdRows) ||
-      !make_map_f16(&v128, p.v, p.B, p.S_kv, p.D_v, tc::kBwdRows) ||
-      !make_map_f16(&q64, p.q, p.B, p.S_q, p.D_qk, tc::kBwdTile) ||
-      !make_map_f16(&do64, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdTile) ||
-      !make_map_f16(&q128, p.q, p.B, p.S_q, p.D_qk, tc::kBwdRows) ||
-      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows) ||
-      !make_map_f16(&k64, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdTile) ||
-      !make_map_f16(&v64, p.v, p.B, p.S_kv, p.D_v, tc::kBwdTile))
-    return SDPA_B200_ECUDA;
-  const int64_t rows = p.B * p.S_q;
-  simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
-  ++t_launches;
-  if (int r = launch_result()) return r;
-  const int64_t gkv = ((p.S_kv + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
-  const int64_t gq = ((p.S_q + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
-  if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kkv<<<static_cast<unsigned>(gkv), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
-  ++t_launches;
-  if (int r = launch_result()) return r;
-  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(q128, do128, k64, v64, p);
-  ++t_launches;
-  return launch_result();
-}
-
-int tc_bwd_dispatch(const Params& p, cudaStream_t st) {
-  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
-  if (q128 && v128) return launch_tc_bwd<128, 128>(p, st);
-  if (q128) return launch_tc_bwd<128, 64>(p, st);
-  if (v128) return launch_tc_bwd<64, 128>(p, st);
-  return launch_tc_bwd<64, 64>(p, st);
 }
 
 bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n) {
@@ -325,8 +135,8 @@ int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* 
   p.out = out;
   p.stats = stats;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (tc_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return tc_fwd_dispatch(p, st);
-  return dtype == SDPA_B200_F16 ? simt_fwd_dispatch<__half>(p, st) : simt_fwd_dispatch<float>(p, st);
+  if (tc_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return launch_fwd_tc(p, st, &t_launches);
+  return dtype == SDPA_B200_F16 ? launch_fwd_simt_f16(p, st, &t_launches) : launch_fwd_simt_f32(p, st, &t_launches);
 }
 
 size_t sdpa_b200_bwd_workspace_bytes(int, int64_t B, int64_t S_q, int64_t, int64_t, int64_t) {
@@ -359,8 +169,8 @@ int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const 
   p.delta = static_cast<float*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
-  if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return tc_bwd_dispatch(p, st);
-  return dtype == SDPA_B200_F16 ? simt_bwd_dispatch<__half>(p, st) : simt_bwd_dispatch<float>(p, st);
+  if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
+  return dtype == SDPA_B200_F16 ? launch_bwd_simt_f16(p, st, &t_launches) : launch_bwd_simt_f32(p, st, &t_launches);
 }
 
 int sdpa_b200_dropout_mask(uint64_t seed, uint64_t offset, int64_t B, int64_t S_q, int64_t S_kv, float dropout,
@@ -394,9 +204,11 @@ int sdpa_b200_device_status(unsigned int* word, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned int w = 0;
   if (cudaStreamSynchronize(st) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (cudaMemcpyFromSymbol(&w, g_status_word, sizeof(w)) != cudaSuccess) return SDPA_B200_ECUDA;
   const unsigned int zero = 0;
+  if (cudaMemcpyFromSymbol(&w, g_status_word, sizeof(w)) != cudaSuccess) return SDPA_B200_ECUDA;
   if (cudaMemcpyToSymbol(g_status_word, &zero, sizeof(zero)) != cudaSuccess) return SDPA_B200_ECUDA;
+  if (status_exchange_fwd_tc(&w) || status_exchange_bwd_tc(&w) || status_exchange_simt_fwd_f16(&w) ||
+      status_exchange_simt_fwd_f32(&w) || status_exchange_simt_bwd_f16(&w) || status_exchange_simt_bwd_f32(&w)) return SDPA_B200_ECUDA;
   if (word) *word = w;
   return (w & kStatusTimeout) ? SDPA_B200_ETIMEOUT : SDPA_B200_OK;
 }

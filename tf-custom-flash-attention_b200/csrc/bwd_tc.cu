@@ -1,0 +1,59 @@
+// Translation unit: tcgen05 backward kernels
+#include "host.cuh"
+#include "ptx.cuh"
+#include "simt.cuh"
+#include "bwd_tc.cuh"
+
+using namespace sdpa_b200;
+using namespace sdpa_b200::host;
+
+namespace {
+
+// tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
+template <int DQK, int DV>
+int launch_tc_bwd(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
+  using Cfg = tc::BwdCfg<DQK, DV>;
+  auto kkv = tc::dkdv_kernel<DQK, DV>;
+  auto kq = tc::dq_kernel<DQK, DV>;
+  if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
+  if (ensure_smem(kq, Cfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
+  CUtensorMap k128, v128, q64, do64, q128, do128, k64, v64;
+  if (!make_map_f16(&k128, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&v128, p.v, p.B, p.S_kv, p.D_v, tc::kBwdRows) ||
+      !make_map_f16(&q64, p.q, p.B, p.S_q, p.D_qk, tc::kBwdTile) ||
+      !make_map_f16(&do64, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdTile) ||
+      !make_map_f16(&q128, p.q, p.B, p.S_q, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows) ||
+      !make_map_f16(&k64, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdTile) ||
+      !make_map_f16(&v64, p.v, p.B, p.S_kv, p.D_v, tc::kBwdTile))
+    return SDPA_B200_ECUDA;
+  const int64_t rows = p.B * p.S_q;
+  simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
+  ++*launches;
+  if (int r = launch_result()) return r;
+  const int64_t gkv = ((p.S_kv + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
+  const int64_t gq = ((p.S_q + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
+  if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kkv<<<static_cast<unsigned>(gkv), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
+  ++*launches;
+  if (int r = launch_result()) return r;
+  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(q128, do128, k64, v64, p);
+  ++*launches;
+  return launch_result();
+}
+
+int tc_bwd_dispatch(const Params& p, cudaStream_t st, int* launches) {
+  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
+  if (q128 && v128) return launch_tc_bwd<128, 128>(p, st, launches);
+  if (q128) return launch_tc_bwd<128, 64>(p, st, launches);
+  if (v128) return launch_tc_bwd<64, 128>(p, st, launches);
+  return launch_tc_bwd<64, 64>(p, st, launches);
+}
+
+
+}  // namespace
+
+int sdpa_b200::launch_bwd_tc(const Params& p, cudaStream_t st, int* launches) { return tc_bwd_dispatch(p, st, launches); }
+
+SDPA_B200_STATUS_EXCHANGE(bwd_tc)

@@ -1,0 +1,43 @@
+// Translation unit: tcgen05 forward kernels
+#include "host.cuh"
+#include "ptx.cuh"
+#include "fwd_tc.cuh"
+
+using namespace sdpa_b200;
+using namespace sdpa_b200::host;
+
+namespace {
+
+// ----------------------------------------------------------------- forward
+template <int DQK, int DV>
+int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tc::FwdCfg<DQK, DV>;
+  auto kern = tc::fwd_kernel<DQK, DV>;
+  if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
+  CUtensorMap mq, mk, mv;
+  if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
+      !make_map_f16(&mv, p.v, p.B, p.S_kv, p.D_v, tc::kBN))
+    return SDPA_B200_ECUDA;
+  const int64_t n_qt = (p.S_q + tc::kBM - 1) / tc::kBM;
+  const int64_t grid = n_qt * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tc::kFwdThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
+  ++*launches;
+  return launch_result();
+}
+
+int tc_fwd_dispatch(const Params& p, cudaStream_t st, int* launches) {
+  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
+  if (q128 && v128) return launch_tc_fwd<128, 128>(p, st, launches);
+  if (q128) return launch_tc_fwd<128, 64>(p, st, launches);
+  if (v128) return launch_tc_fwd<64, 128>(p, st, launches);
+  return launch_tc_fwd<64, 64>(p, st, launches);
+}
+
+
+}  // namespace
+
+int sdpa_b200::launch_fwd_tc(const Params& p, cudaStream_t st, int* launches) { return tc_fwd_dispatch(p, st, launches); }
+
+SDPA_B200_STATUS_EXCHANGE(fwd_tc)

@@ -10,8 +10,9 @@
 namespace sdpa_b200 {
 
 // ------------------------------------------------------------ status word
-// Bit 0: a bounded wait gave up.  One word per device (static __device__).
-__device__ unsigned int g_status_word;
+// Bit 0: a bounded wait gave up.  One word per device and translation unit
+// (static: each .cu file's kernels raise their own; the C ABI reads them all).
+static __device__ unsigned int g_status_word;
 constexpr unsigned int kStatusTimeout = 1u;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
