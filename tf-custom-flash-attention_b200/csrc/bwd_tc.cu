@@ -10,12 +10,12 @@ using namespace sdpa_b200::host;
 namespace {
 
 // tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
-template <int DQK, int DV>
-int launch_tc_bwd(const Params& p, cudaStream_t st, int* launches) {
+template <int DQK, int DV, bool DROP>
+int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
   using Cfg = tc::BwdCfg<DQK, DV>;
-  auto kkv = tc::dkdv_kernel<DQK, DV>;
-  auto kq = tc::dq_kernel<DQK, DV>;
+  auto kkv = tc::dkdv_kernel<DQK, DV, DROP>;
+  auto kq = tc::dq_kernel<DQK, DV, DROP>;
   if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
   if (ensure_smem(kq, Cfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
   CUtensorMap k128, v128, q64, do64, q128, do128, k64, v64;
@@ -41,6 +41,11 @@ int launch_tc_bwd(const Params& p, cudaStream_t st, int* launches) {
   kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(q128, do128, k64, v64, p);
   ++*launches;
   return launch_result();
+}
+
+template <int DQK, int DV>
+int launch_tc_bwd(const Params& p, cudaStream_t st, int* launches) {
+  return p.dropout_on ? launch_tc_bwd_t<DQK, DV, true>(p, st, launches) : launch_tc_bwd_t<DQK, DV, false>(p, st, launches);
 }
 
 int tc_bwd_dispatch(const Params& p, cudaStream_t st, int* launches) {

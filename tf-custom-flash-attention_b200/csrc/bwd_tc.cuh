@@ -69,30 +69,6 @@ struct BwdBarriers {
   int abort_flag;
 };
 
-// Elementwise gradient of one score: inputs s (raw dot product), dP, the
-// row terms; outputs the dropped-out probability (for dV) and the unscaled dS.
-struct GradTerms {
-  float scale_log2, dp_inv;
-  uint64_t thr;
-  int dropout_on;
-};
-__device__ __forceinline__ void grad_elem(const GradTerms& g, bool valid, float s, float dp, float lse2, float delta,
-                                          float delta_k, uint64_t state, float& pt, float& ds) {
-  float p = ex2(fmaf(s, g.scale_log2, -lse2));
-  if (!valid || !(p > kEps)) {  // masked, or skipped as in sdpa/sdpa_bwd.cu.cc:131
-    pt = 0.0f;
-    ds = 0.0f;
-    return;
-  }
-  if (g.dropout_on && dropped(state, g.thr)) {
-    pt = 0.0f;
-    ds = -p * delta;
-    return;
-  }
-  pt = p * g.dp_inv;
-  ds = pt * (dp - delta_k);
-}
-
 // Shared prologue of both backward kernels: barriers, TMEM, wait control.
 __device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols, int warp) {
   if (threadIdx.x == 0) {
@@ -215,7 +191,7 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, int nchunks, int c
   }
 }
 
-template <int DQK, int DV>
+template <int DQK, int DV, bool DROP>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do, const Params p) {
@@ -286,11 +262,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int col0 = half * 32;
     const int64_t j = n0 + r;                 // key row
     float* vec = reinterpret_cast<float*>(smem + Cfg::kVecOff);  // [2][3][64]
-    GradTerms g;
-    g.scale_log2 = p.scale_log2;
-    g.dp_inv = p.dp_inv;
-    g.thr = p.drop_thr;
-    g.dropout_on = p.dropout_on;
+    const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
+    const bool all_drop = p.drop_thr > 0xffffffffull;
+    const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
+    const int64_t jw0 = n0 + (warp & 3) * 32;  // first key row of this warp
     const uint64_t step_i = static_cast<uint64_t>(p.S_kv) * kLcgA;  // counter step between query rows
     auto row_val = [&](int t) -> float {      // this thread's share of tile t's row vectors
       const int64_t i = static_cast<int64_t>(tile0 + t) * kBwdTile + (e & 63);
@@ -319,20 +294,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dpv);
       tmem_wait_ld();
       const int64_t i0 = static_cast<int64_t>(tile0 + t) * kBwdTile + col0;
-      uint64_t st = lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i0) * static_cast<uint64_t>(p.S_kv),
-                              static_cast<uint64_t>(j));
+      // causal: column c is valid iff i0 + c >= j; only warps on the diagonal test it
+      int lo = -1;
+      if (p.causal && i0 < jw0 + 31) {
+        const int64_t d = j - i0;
+        lo = static_cast<int>(d < -1 ? -1 : (d > 32 ? 32 : d));
+      }
+      uint64_t st = 0;
+      if (DROP)
+        st = lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i0) * static_cast<uint64_t>(p.S_kv),
+                       static_cast<uint64_t>(j));
       uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        float pt0, ds0, pt1, ds1;
-        grad_elem(g, !p.causal || i0 + c >= j, __uint_as_float(sv[c]), __uint_as_float(dpv[c]), vb[col0 + c],
-                  vb[kBwdTile + col0 + c], vb[2 * kBwdTile + col0 + c], st, pt0, ds0);
-        st += step_i;
-        grad_elem(g, !p.causal || i0 + c + 1 >= j, __uint_as_float(sv[c + 1]), __uint_as_float(dpv[c + 1]),
-                  vb[col0 + c + 1], vb[kBwdTile + col0 + c + 1], vb[2 * kBwdTile + col0 + c + 1], st, pt1, ds1);
-        st += step_i;
-        pk[c / 2] = pack_half2(pt0, pt1);
-        dk[c / 2] = pack_half2(ds0, ds1);
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 L4 = *reinterpret_cast<const float4*>(vb + col0 + 4 * c4);
+        const float4 D4 = *reinterpret_cast<const float4*>(vb + kBwdTile + col0 + 4 * c4);
+        const float4 K4 = *reinterpret_cast<const float4*>(vb + 2 * kBwdTile + col0 + 4 * c4);
+        const float Lv[4] = {L4.x, L4.y, L4.z, L4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w},
+                    Kv[4] = {K4.x, K4.y, K4.z, K4.w};
+        float ptv[4], dsv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * c4 + e;
+          float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -Lv[e]));
+          pr = (pr > kEps && c >= lo) ? pr : 0.0f;  // skip rule of sdpa/sdpa_bwd.cu.cc:131, causal mask
+          const float dpc = __uint_as_float(dpv[c]);
+          if (DROP) {
+            const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
+            st += step_i;
+            ptv[e] = dr ? 0.0f : pr * dp_inv;
+            dsv[e] = dr ? -pr * Dv[e] : ptv[e] * (dpc - Kv[e]);
+          } else {
+            ptv[e] = pr;
+            dsv[e] = pr * (dpc - Dv[e]);
+          }
+        }
+        pk[2 * c4] = pack_half2(ptv[0], ptv[1]);
+        pk[2 * c4 + 1] = pack_half2(ptv[2], ptv[3]);
+        dk[2 * c4] = pack_half2(dsv[0], dsv[1]);
+        dk[2 * c4 + 1] = pack_half2(dsv[2], dsv[3]);
       }
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, pk);
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-template <int DQK, int DV>
+template <int DQK, int DV, bool DROP>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -432,11 +432,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
     const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
     const float delta_k = delta / p.dp_inv;
-    GradTerms g;
-    g.scale_log2 = p.scale_log2;
-    g.dp_inv = p.dp_inv;
-    g.thr = p.drop_thr;
-    g.dropout_on = p.dropout_on;
+    const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
+    const bool all_drop = p.drop_thr > 0xffffffffull;
+    const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
     const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv);
     bool ok = true;
     for (int t = 0; t < nkv; ++t) {
@@ -454,17 +452,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int64_t lim64 = p.S_kv - j0;
       if (p.causal) lim64 = min(lim64, i - j0 + 1);
       const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
-      uint64_t st = lcg_state(rbase, static_cast<uint64_t>(j0));
+      uint64_t st = DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0;
       uint32_t dk[16];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
-        float pt0, ds0, pt1, ds1;
-        grad_elem(g, c < lim, __uint_as_float(sv[c]), __uint_as_float(dpv[c]), lse2, delta, delta_k, st, pt0, ds0);
-        st += kLcgA;
-        grad_elem(g, c + 1 < lim, __uint_as_float(sv[c + 1]), __uint_as_float(dpv[c + 1]), lse2, delta, delta_k, st,
-                  pt1, ds1);
-        st += kLcgA;
-        dk[c / 2] = pack_half2(ds0, ds1);
+        float dsv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float pr = ex2(fmaf(__uint_as_float(sv[c + e]), sl2, -lse2));
+          pr = (pr > kEps && c + e < lim) ? pr : 0.0f;  // skip rule, key range, causal mask
+          const float dpc = __uint_as_float(dpv[c + e]);
+          if (DROP) {
+            const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
+            st += kLcgA;
+            const float pt = pr * dp_inv;
+            dsv[e] = dr ? -pr * delta : pt * (dpc - delta_k);
+          } else {
+            dsv[e] = pr * (dpc - delta);
+          }
+        }
+        dk[c / 2] = pack_half2(dsv[0], dsv[1]);
       }
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
       tmem_wait_st();

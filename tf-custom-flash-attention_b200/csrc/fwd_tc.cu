@@ -9,11 +9,11 @@ using namespace sdpa_b200::host;
 namespace {
 
 // ----------------------------------------------------------------- forward
-template <int DQK, int DV>
-int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
+template <int DQK, int DV, bool DROP>
+int launch_tc_fwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tc::FwdCfg<DQK, DV>;
-  auto kern = tc::fwd_kernel<DQK, DV>;
+  auto kern = tc::fwd_kernel<DQK, DV, DROP>;
   if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
   CUtensorMap mq, mk, mv;
   if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
@@ -25,6 +25,11 @@ int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
   kern<<<static_cast<unsigned>(grid), tc::kFwdThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
   ++*launches;
   return launch_result();
+}
+
+template <int DQK, int DV>
+int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
+  return p.dropout_on ? launch_tc_fwd_t<DQK, DV, true>(p, st, launches) : launch_tc_fwd_t<DQK, DV, false>(p, st, launches);
 }
 
 int tc_fwd_dispatch(const Params& p, cudaStream_t st, int* launches) {

@@ -85,7 +85,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
   return raw + ((1024u - (a & 1023u)) & 1023u);
 }
 
-template <int DQK, int DV>
+template <int DQK, int DV, bool DROP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -246,16 +246,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       SDPA_TMEM_LD32(tmem + lane_base + s * 128 + 96, (r + 96));
       tmem_wait_ld();
       const int64_t kv0 = static_cast<int64_t>(j) * kBN;
-      int64_t lim64 = p.S_kv - kv0;
-      if (p.causal) lim64 = min(lim64, row - kv0 + 1);
-      const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kBN ? kBN : lim64));
-      float tmax = -INFINITY;
+      // Scale is folded into one FFMA per element when positive (max over the
+      // raw scores); otherwise the scores are scaled first.
+      const bool fold = p.scale_log2 > 0.0f;
+      const float sl = fold ? p.scale_log2 : 1.0f;
+      if (!fold) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float x = (c < lim) ? __uint_as_float(r[c]) * p.scale_log2 : -INFINITY;
-        r[c] = __float_as_uint(x);
-        tmax = fmaxf(tmax, x);
+        for (int c = 0; c < 128; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * p.scale_log2);
       }
+      // Masking only where this warp's rows meet the key range or the diagonal.
+      const int64_t row_w0 = m0 + warp * 32;
+      const bool edge = (kv0 + kBN > p.S_kv) || (p.causal && kv0 + kBN - 1 > row_w0);
+      if (edge) {
+        int64_t lim64 = p.S_kv - kv0;
+        if (p.causal) lim64 = min(lim64, row - kv0 + 1);
+        const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kBN ? kBN : lim64));
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= lim) r[c] = __float_as_uint(-INFINITY);
+      }
+      float tmax_raw = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) tmax_raw = fmaxf(tmax_raw, __uint_as_float(r[c]));
+      const float tmax = tmax_raw * sl;
       m_run = fmaxf(m_run, tmax);
       float alpha = 1.0f;
       bool rescale_o = false;
@@ -268,24 +281,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float mu = (m_use == -INFINITY) ? 0.0f : m_use;
       float rs = 0.0f;
       uint32_t pk[64];
-      if (p.dropout_on) {
+      if (DROP) {
         uint64_t st = lcg_state(rbase, static_cast<uint64_t>(kv0));
+        const bool all_drop = p.drop_thr > 0xffffffffull;
+        const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
-          float p0 = ex2(__uint_as_float(r[c]) - mu);
-          float p1 = ex2(__uint_as_float(r[c + 1]) - mu);
+          float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
+          float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
           rs += p0 + p1;
-          if (dropped(st, p.drop_thr)) p0 = 0.0f;
+          const bool d0 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
           st += kLcgA;
-          if (dropped(st, p.drop_thr)) p1 = 0.0f;
+          const bool d1 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
           st += kLcgA;
-          pk[c / 2] = pack_half2(p0, p1);
+          pk[c / 2] = pack_half2(d0 ? 0.0f : p0, d1 ? 0.0f : p1);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
-          const float p0 = ex2(__uint_as_float(r[c]) - mu);
-          const float p1 = ex2(__uint_as_float(r[c + 1]) - mu);
+          const float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
+          const float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
           rs += p0 + p1;
           pk[c / 2] = pack_half2(p0, p1);
         }
