@@ -3,6 +3,8 @@
 #include "ptx.cuh"
 #include "fwd_tc.cuh"
 
+#include <cstdlib>
+
 using namespace sdpa_b200;
 using namespace sdpa_b200::host;
 
@@ -32,7 +34,41 @@ int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
   return p.dropout_on ? launch_tc_fwd_t<DQK, DV, true>(p, st, launches) : launch_tc_fwd_t<DQK, DV, false>(p, st, launches);
 }
 
+// Paired-tile forward (two 128-row query tiles per CTA).
+template <int DQK, int DV, bool DROP>
+int launch_pair_fwd_t(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tc::PairCfg<DQK, DV>;
+  auto kern = tc::fwd_pair_kernel<DQK, DV, DROP>;
+  if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
+  CUtensorMap mq, mk, mv;
+  if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
+      !make_map_f16(&mv, p.v, p.B, p.S_kv, p.D_v, tc::kBN))
+    return SDPA_B200_ECUDA;
+  const int64_t grid = ((p.S_q + 2 * tc::kBM - 1) / (2 * tc::kBM)) * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tc::kPairThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
+  ++*launches;
+  return launch_result();
+}
+
+template <int DQK, int DV>
+int launch_pair_fwd(const Params& p, cudaStream_t st, int* launches) {
+  // A single 128-row query tile per batch row leaves half of a pair idle:
+  // the one-tile kernel serves those shapes.
+  if (p.S_q <= tc::kBM) return launch_tc_fwd<DQK, DV>(p, st, launches);
+  return p.dropout_on ? launch_pair_fwd_t<DQK, DV, true>(p, st, launches)
+                      : launch_pair_fwd_t<DQK, DV, false>(p, st, launches);
+}
+
 int tc_fwd_dispatch(const Params& p, cudaStream_t st, int* launches) {
+  if (!std::getenv("SDPA_B200_FWD_SINGLE")) {
+    const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
+    if (q128 && v128) return launch_pair_fwd<128, 128>(p, st, launches);
+    if (q128) return launch_pair_fwd<128, 64>(p, st, launches);
+    if (v128) return launch_pair_fwd<64, 128>(p, st, launches);
+    return launch_pair_fwd<64, 64>(p, st, launches);
+  }
   const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
   if (q128 && v128) return launch_tc_fwd<128, 128>(p, st, launches);
   if (q128) return launch_tc_fwd<128, 64>(p, st, launches);
