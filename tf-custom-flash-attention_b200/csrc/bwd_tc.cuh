@@ -44,7 +44,7 @@ struct BwdCfg {
   static constexpr uint32_t kStAOff = kResBOff + kResB;
   static constexpr uint32_t kStBOff = kStAOff + kBwdStages * kStA;
   static constexpr uint32_t kVecOff = kStBOff + kBwdStages * kStB;  // per-tile row vectors
-  static constexpr uint32_t kVecBytes = 2 * 3 * kBwdTile * 4;       // 2 buffers x {lse2, delta, delta/dp_inv}
+  static constexpr uint32_t kVecBytes = 2 * 2 * kBwdTile * 4;       // 2 buffers x {lse2, delta}
   static constexpr uint32_t kBarOff = kVecOff + kVecBytes;
   static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
   static constexpr uint32_t kTmemCols = 512;
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int col0 = half * 32;
     const int64_t j = n0 + r;                 // key row
-    float* vec = reinterpret_cast<float*>(smem + Cfg::kVecOff);  // [2][3][64]
+    float* vec = reinterpret_cast<float*>(smem + Cfg::kVecOff);  // [2][2][64]
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
     const bool all_drop = p.drop_thr > 0xffffffffull;
     const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
@@ -270,18 +270,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     auto row_val = [&](int t) -> float {      // this thread's share of tile t's row vectors
       const int64_t i = static_cast<int64_t>(tile0 + t) * kBwdTile + (e & 63);
       const int which = e >> 6;
-      if (which >= 3) return 0.0f;
+      if (which >= 2) return 0.0f;
       if (i >= p.S_q) return which == 0 ? INFINITY : 0.0f;
-      if (which == 0) return p.lse[b * p.S_q + i] * kLog2e;
-      const float d = p.delta[b * p.S_q + i];
-      return which == 1 ? d : d / p.dp_inv;
+      return which == 0 ? p.lse[b * p.S_q + i] * kLog2e : p.delta[b * p.S_q + i];
     };
     float pre = nq > 0 ? row_val(0) : 0.0f;
     bool ok = true;
     for (int t = 0; t < nq; ++t) {
       const int sb = t & 1;
-      float* vb = vec + sb * 3 * kBwdTile;
-      if (e < 3 * kBwdTile) vb[e] = pre;
+      float* vb = vec + sb * 2 * kBwdTile;
+      if (e < 2 * kBwdTile) vb[e] = pre;
       mbar_arrive(&bars->vec_ready[sb]);
       if (t + 1 < nq) pre = row_val(t + 1);
       if (!warp_wait(&bars->vec_ready[sb], (t >> 1) & 1, ctl) || !warp_wait(&bars->s_full[sb], (t >> 1) & 1, ctl)) {
@@ -309,9 +307,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c4 = 0; c4 < 8; ++c4) {
         const float4 L4 = *reinterpret_cast<const float4*>(vb + col0 + 4 * c4);
         const float4 D4 = *reinterpret_cast<const float4*>(vb + kBwdTile + col0 + 4 * c4);
-        const float4 K4 = *reinterpret_cast<const float4*>(vb + 2 * kBwdTile + col0 + 4 * c4);
-        const float Lv[4] = {L4.x, L4.y, L4.z, L4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w},
-                    Kv[4] = {K4.x, K4.y, K4.z, K4.w};
+        const float Lv[4] = {L4.x, L4.y, L4.z, L4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w};
         float ptv[4], dsv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -319,15 +315,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -Lv[e]));
           pr = (pr > kEps && c >= lo) ? pr : 0.0f;  // skip rule of sdpa/sdpa_bwd.cu.cc:131, causal mask
           const float dpc = __uint_as_float(dpv[c]);
+          // dropped: P~ = 0, dS = -p D; kept: P~ = p/(1-r), dS = P~ (dP - D (1-r)) = p (dP/(1-r) - D)
+          float kf = 1.0f;
           if (DROP) {
             const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
             st += step_i;
-            ptv[e] = dr ? 0.0f : pr * dp_inv;
-            dsv[e] = dr ? -pr * Dv[e] : ptv[e] * (dpc - Kv[e]);
-          } else {
-            ptv[e] = pr;
-            dsv[e] = pr * (dpc - Dv[e]);
+            kf = dr ? 0.0f : dp_inv;
           }
+          ptv[e] = pr * kf;
+          dsv[e] = pr * fmaf(kf, dpc, -Dv[e]);
         }
         pk[2 * c4] = pack_half2(ptv[0], ptv[1]);
         pk[2 * c4 + 1] = pack_half2(ptv[2], ptv[3]);
@@ -431,7 +427,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const bool row_ok = i < p.S_q;
     const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
     const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
-    const float delta_k = delta / p.dp_inv;
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
     const bool all_drop = p.drop_thr > 0xffffffffull;
     const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
@@ -462,14 +457,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           float pr = ex2(fmaf(__uint_as_float(sv[c + e]), sl2, -lse2));
           pr = (pr > kEps && c + e < lim) ? pr : 0.0f;  // skip rule, key range, causal mask
           const float dpc = __uint_as_float(dpv[c + e]);
+          float kf = 1.0f;  // see the dK/dV kernel: dS = p (kf dP - D)
           if (DROP) {
             const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
             st += kLcgA;
-            const float pt = pr * dp_inv;
-            dsv[e] = dr ? -pr * delta : pt * (dpc - delta_k);
-          } else {
-            dsv[e] = pr * (dpc - delta);
+            kf = dr ? 0.0f : dp_inv;
           }
+          dsv[e] = pr * fmaf(kf, dpc, -delta);
         }
         dk[c / 2] = pack_half2(dsv[0], dsv[1]);
       }
