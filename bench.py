@@ -230,12 +230,17 @@ def run_ours(args, w):
     total_ms = e0.elapsed_time(prev)
     fwd_ms = sum(a.elapsed_time(m) for a, m, _ in evs) / args.steps
     bwd_ms = sum(m.elapsed_time(e) for _, m, e in evs) / args.steps
+    clk = clocks.stop()
+    per_rank = [{"rank": rank, "ms_per_step": total_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
+                 "reasons": clk.get("reasons")}]
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms = float(t.item())
+        gathered = [None] * world
+        torch.distributed.all_gather_object(gathered, per_rank[0])
+        per_rank = gathered
         torch.distributed.barrier()
-    clk = clocks.stop()
 
     # ---- end to end through the public API: pinned host inputs in, results out, every step
     hq, hk, hv, hdo = (x.cpu().pin_memory() for x in (q, k, v, do))
@@ -315,6 +320,7 @@ def run_ours(args, w):
         "e2e": {"value": world * (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": launches[0],
+        "per_rank": per_rank,
         "clocks": clk,
         "cpu_baseline": cpu,
     }
