@@ -37,16 +37,27 @@ WORKLOADS = {
     "cfg4": dict(B=32, S=8192, D_qk=128, D_v=128, causal=True, dropout=0.1, seed=7, offset=0, dtype="f16"),
     "cfg3": dict(B=256, S=2048, D_qk=128, D_v=128, causal=False, dropout=0.0, seed=0, offset=0, dtype="f16"),
     "cfg2": dict(B=64, S=1024, D_qk=64, D_v=64, causal=True, dropout=0.0, seed=0, offset=0, dtype="f16"),
+    # fp32 cases (BASELINE.json configs[0] and [4])
+    "cfg1": dict(B=20, S=400, D_qk=32, D_v=4, causal=False, dropout=0.2, seed=42, offset=1000, dtype="f32"),
+    "cfg5": dict(B=128, S=512, S_kv=4096, D_qk=64, D_v=128, causal=False, dropout=0.05, seed=0, offset=0,
+                 dtype="f32", std=0.5),
 }
 METRIC = "fwd and fwd+bwd attention TFLOP/s per B200, % of dense fp16 tensor peak"
 
 
-def flops(w, B=None, S=None):
+def seqs(w):
+    """(S_q, S_kv) of a workload."""
+    return w["S"], w.get("S_kv", w["S"])
+
+
+def flops(w, B=None, S_q=None, S_kv=None):
     B = w["B"] if B is None else B
-    S = w["S"] if S is None else S
+    sq, skv = seqs(w)
+    S_q = sq if S_q is None else S_q
+    S_kv = skv if S_kv is None else S_kv
     f = 0.5 if w["causal"] else 1.0
-    fwd = 2.0 * S * S * (w["D_qk"] + w["D_v"]) * B * f
-    bwd = 2.0 * S * S * (3 * w["D_qk"] + 2 * w["D_v"]) * B * f
+    fwd = 2.0 * S_q * S_kv * (w["D_qk"] + w["D_v"]) * B * f
+    bwd = 2.0 * S_q * S_kv * (3 * w["D_qk"] + 2 * w["D_v"]) * B * f
     return fwd, bwd
 
 
@@ -132,7 +143,8 @@ def cpu_sample(w):
     from oracle import ref
 
     threads = ref.get_num_threads("CPU")
-    return dict(B=threads, S=min(w["S"], 1024)), threads
+    sq, skv = seqs(w)
+    return dict(B=threads, S_q=min(sq, 1024), S_kv=min(skv, 1024)), threads
 
 
 def time_reference_cpu(w, steps=1):
@@ -142,10 +154,12 @@ def time_reference_cpu(w, steps=1):
     from oracle import ref
 
     smp, threads = cpu_sample(w)
-    B, S = smp["B"], smp["S"]
+    B, S_q, S_kv = smp["B"], smp["S_q"], smp["S_kv"]
     rng = np.random.default_rng(0)
     dt = np.float16 if w["dtype"] == "f16" else np.float32
-    q, k, v, do = (rng.standard_normal((B, S, d)).astype(dt) for d in (w["D_qk"], w["D_qk"], w["D_v"], w["D_v"]))
+    std = w.get("std", 1.0)
+    q, k, v, do = ((rng.standard_normal(shape) * std).astype(dt) for shape in
+                   ((B, S_q, w["D_qk"]), (B, S_kv, w["D_qk"]), (B, S_kv, w["D_v"]), (B, S_q, w["D_v"])))
     kw = dict(scale=w["D_qk"] ** -0.5, dropout=w["dropout"], causal_mask=w["causal"])
     times = []
     for _ in range(steps):
@@ -153,10 +167,10 @@ def time_reference_cpu(w, steps=1):
         o, s = ref.ref_sdpa(q, k, v, w["seed"], w["offset"], **kw)
         ref.ref_sdpa_grad(q, k, v, o, s, do, w["seed"], w["offset"], **kw)
         times.append(time.perf_counter() - t0)
-    f, b = flops(w, B, S)
+    f, b = flops(w, B, S_q, S_kv)
     t = statistics.median(times)
-    sample = (f"reference CPU op (sdpa/sdpa_cpu.cc, -O2) fwd+bwd on [{B},{S},{w['D_qk']}] "
-              f"(S reduced from {w['S']}, one batch row per thread), {w['dtype']}, "
+    sample = (f"reference CPU op (sdpa/sdpa_cpu.cc, -O2) fwd+bwd on q[{B},{S_q},{w['D_qk']}] "
+              f"kv[{B},{S_kv},{w['D_qk']}/{w['D_v']}] (sequences capped at 1024, one batch row per thread), {w['dtype']}, "
               f"causal={w['causal']}, dropout={w['dropout']}")
     return (f + b) / t / 1e12, threads, sample, t
 
@@ -172,7 +186,8 @@ def run_reference(args, w):
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, **{k: w[k] for k in ("B", "S", "D_qk", "D_v", "causal", "dropout")}},
+        "config": {"workload": args.workload, **{k: w[k] for k in ("B", "S", "D_qk", "D_v", "causal", "dropout")},
+                   "S_kv": seqs(w)[1]},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -186,13 +201,15 @@ def run_ours(args, w):
     torch.cuda.set_device(local)
     fa = importlib.import_module("tf-custom-flash-attention_b200")
     dev = torch.device("cuda", local)
-    B, S, Dq, Dv = w["B"], w["S"], w["D_qk"], w["D_v"]
+    B, Dq, Dv = w["B"], w["D_qk"], w["D_v"]
+    S, S_kv = seqs(w)
     dt = torch.float16 if w["dtype"] == "f16" else torch.float32
     b0 = rank * B  # weak scaling: this rank's global batch rows
-    offset = fa.sharding.shard_offset(w["offset"], b0, S, S)
+    offset = fa.sharding.shard_offset(w["offset"], b0, S, S_kv)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    q, k, v, do = (torch.randn((B, S, d), generator=g, device=dev, dtype=torch.float32).to(dt)
-                   for d in (Dq, Dq, Dv, Dv))
+    std = w.get("std", 1.0)
+    q, k, v, do = ((torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(dt)
+                   for shape in ((B, S, Dq), (B, S_kv, Dq), (B, S_kv, Dv), (B, S, Dv)))
     kw = dict(scale=Dq ** -0.5, dropout=w["dropout"], causal_mask=w["causal"])
     stream = torch.cuda.current_stream()
 
@@ -310,9 +327,12 @@ def run_ours(args, w):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16" if dt == torch.float16 else "f32", "data": "synthetic (seeded N(0,1))",
         "config": {"workload": args.workload, "global_batch": B * world, "per_gpu_batch": B, "seq_len": S,
+                   "seq_len_kv": S_kv,
                    "D_qk": Dq, "D_v": Dv, "causal": w["causal"], "dropout": w["dropout"],
                    "parallelism": f"batch-sharded x{world}, no collective",
-                   "l2": f"inputs larger than L2 ({4 * B * S * Dq * 2 / 1e6:.0f} MB per step)"},
+                   "l2": (f"inputs {sum(x.numel() * x.element_size() for x in (q, k, v, do)) / 1e6:.0f} MB per step "
+                          + ("(larger than L2)" if sum(x.numel() * x.element_size() for x in (q, k, v, do)) > 126e6
+                             else "(fit in L2: small config)"))},
         "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf, "pct_of_peak": 100.0 * value / world / peak,
         "roofline": {"bound": "tensor", "kernel": dominant[0], "achieved": dominant[1], "peak": peak,
                      "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": dominant[1] / peak, "traffic": traffic,
