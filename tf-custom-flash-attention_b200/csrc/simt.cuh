@@ -133,8 +133,19 @@ __device__ __forceinline__ bool elem_grad(const Params& p, float s_log2, float l
   return true;
 }
 
+// Threads per key row in dkdv_kernel: wide head dims split the dK / dV
+// accumulators over two threads (partial dot products joined by a shuffle)
+// so they stay in registers.
+template <int DM>
+__host__ __device__ constexpr int dkdv_split() {
+  return DM >= 64 ? 2 : 1;
+}
+
 template <typename T, int DM>
-__global__ void __launch_bounds__(kBwdRows) dkdv_kernel(Params p) {
+__global__ void __launch_bounds__(kBwdRows * dkdv_split<DM>()) dkdv_kernel(Params p) {
+  constexpr int SPLIT = dkdv_split<DM>();
+  constexpr int DH = DM / SPLIT;              // head-dim slice owned by this thread
+  constexpr int NT = kBwdRows * SPLIT;
   extern __shared__ float sm[];
   float* Kt = sm;                         // [DM][kBwdRows]
   float* Vt = Kt + DM * kBwdRows;         // [DM][kBwdRows]
@@ -142,54 +153,62 @@ __global__ void __launch_bounds__(kBwdRows) dkdv_kernel(Params p) {
   float* dOs = Qs + kBwdTile * DM;        // [kBwdTile][DM]
   float* lse_s = dOs + kBwdTile * DM;     // [kBwdTile] (log2 units)
   float* del_s = lse_s + kBwdTile;        // [kBwdTile]
-  const int64_t n_kt = (p.S_kv + kBwdRows - 1) / kBwdRows;
   const int64_t b = blockIdx.x % p.B;
   const int64_t kt = blockIdx.x / p.B;
   const int tid = threadIdx.x;
-  const int64_t kv = kt * kBwdRows + tid;
+  const int r = tid / SPLIT, h = tid % SPLIT, d0 = h * DH;
+  const int64_t kv = kt * kBwdRows + r;
   const bool active = kv < p.S_kv;
-  (void)n_kt;
   const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
   const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
   const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
   const T* dO = static_cast<const T*>(p.d_o) + b * p.S_q * p.D_v;
-  for (int d = 0; d < DM; ++d) {
-    Kt[d * kBwdRows + tid] = (active && d < p.D_qk) ? to_f<T>(K[kv * p.D_qk + d]) : 0.0f;
-    Vt[d * kBwdRows + tid] = (active && d < p.D_v) ? to_f<T>(V[kv * p.D_v + d]) : 0.0f;
+  for (int idx = tid; idx < DM * kBwdRows; idx += NT) {
+    const int d = idx / kBwdRows, rr = idx - d * kBwdRows;
+    const int64_t kvr = kt * kBwdRows + rr;
+    Kt[idx] = (kvr < p.S_kv && d < p.D_qk) ? to_f<T>(K[kvr * p.D_qk + d]) : 0.0f;
+    Vt[idx] = (kvr < p.S_kv && d < p.D_v) ? to_f<T>(V[kvr * p.D_v + d]) : 0.0f;
   }
-  float dk[DM], dv[DM];
+  float dk[DH], dv[DH];
 #pragma unroll
-  for (int d = 0; d < DM; ++d) dk[d] = dv[d] = 0.0f;
+  for (int d = 0; d < DH; ++d) dk[d] = dv[d] = 0.0f;
   const int64_t q_start = p.causal ? (kt * kBwdRows / kBwdTile) * kBwdTile : 0;
   for (int64_t q0 = q_start; q0 < p.S_q; q0 += kBwdTile) {
     __syncthreads();
-    stage_rows<T>(Qs, Q, q0, p.S_q, kBwdTile, p.D_qk, DM, tid, kBwdRows);
-    stage_rows<T>(dOs, dO, q0, p.S_q, kBwdTile, p.D_v, DM, tid, kBwdRows);
-    for (int r = tid; r < kBwdTile; r += kBwdRows) {
-      const int64_t i = q0 + r;
-      lse_s[r] = i < p.S_q ? p.lse[b * p.S_q + i] * kLog2e : 0.0f;
-      del_s[r] = i < p.S_q ? p.delta[b * p.S_q + i] : 0.0f;
+    stage_rows<T>(Qs, Q, q0, p.S_q, kBwdTile, p.D_qk, DM, tid, NT);
+    stage_rows<T>(dOs, dO, q0, p.S_q, kBwdTile, p.D_v, DM, tid, NT);
+    for (int rr = tid; rr < kBwdTile; rr += NT) {
+      const int64_t i = q0 + rr;
+      lse_s[rr] = i < p.S_q ? p.lse[b * p.S_q + i] * kLog2e : 0.0f;
+      del_s[rr] = i < p.S_q ? p.delta[b * p.S_q + i] : 0.0f;
     }
     __syncthreads();
-    if (!active) continue;
-    for (int r = 0; r < kBwdTile; ++r) {
-      const int64_t i = q0 + r;
+    if (!active) continue;  // both threads of a row take the same path
+    for (int rr = 0; rr < kBwdTile; ++rr) {
+      const int64_t i = q0 + rr;
       if (i >= p.S_q) break;
       if (p.causal && i < kv) continue;
       float s = 0.0f, dP = 0.0f;
 #pragma unroll
-      for (int d = 0; d < DM; ++d) s = fmaf(Qs[r * DM + d], Kt[d * kBwdRows + tid], s);
+      for (int d = 0; d < DH; ++d) s = fmaf(Qs[rr * DM + d0 + d], Kt[(d0 + d) * kBwdRows + r], s);
 #pragma unroll
-      for (int d = 0; d < DM; ++d) dP = fmaf(dOs[r * DM + d], Vt[d * kBwdRows + tid], dP);
+      for (int d = 0; d < DH; ++d) dP = fmaf(dOs[rr * DM + d0 + d], Vt[(d0 + d) * kBwdRows + r], dP);
+      if (SPLIT == 2) {
+        // Only the two threads of this key row are guaranteed to be here (rows
+        // of a warp skip different query rows), so the shuffle names just them.
+        const unsigned pair = 0x3u << (threadIdx.x & 30);
+        s += __shfl_xor_sync(pair, s, 1);
+        dP += __shfl_xor_sync(pair, dP, 1);
+      }
       const uint64_t st =
           lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv),
                     static_cast<uint64_t>(kv));
       float pr, dS;
-      if (!elem_grad(p, s * p.scale_log2, lse_s[r], del_s[r], st, dP, pr, dS)) continue;
+      if (!elem_grad(p, s * p.scale_log2, lse_s[rr], del_s[rr], st, dP, pr, dS)) continue;
 #pragma unroll
-      for (int d = 0; d < DM; ++d) {
-        dv[d] = fmaf(pr, dOs[r * DM + d], dv[d]);
-        dk[d] = fmaf(dS, Qs[r * DM + d], dk[d]);
+      for (int d = 0; d < DH; ++d) {
+        dv[d] = fmaf(pr, dOs[rr * DM + d0 + d], dv[d]);
+        dk[d] = fmaf(dS, Qs[rr * DM + d0 + d], dk[d]);
       }
     }
   }
@@ -197,9 +216,9 @@ __global__ void __launch_bounds__(kBwdRows) dkdv_kernel(Params p) {
   T* dK = static_cast<T*>(p.dk) + (b * p.S_kv + kv) * p.D_qk;
   T* dV = static_cast<T*>(p.dv) + (b * p.S_kv + kv) * p.D_v;
 #pragma unroll
-  for (int d = 0; d < DM; ++d) {
-    if (d < p.D_qk) dK[d] = from_f<T>(dk[d]);
-    if (d < p.D_v) dV[d] = from_f<T>(dv[d]);
+  for (int d = 0; d < DH; ++d) {
+    if (d0 + d < p.D_qk) dK[d0 + d] = from_f<T>(dk[d]);
+    if (d0 + d < p.D_v) dV[d0 + d] = from_f<T>(dv[d]);
   }
 }
 

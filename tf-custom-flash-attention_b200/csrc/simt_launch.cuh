@@ -46,7 +46,7 @@ int launch_simt_bwd(const Params& p, cudaStream_t st, int* launches) {
   const int64_t gq = ((p.S_q + simt::kBwdRows - 1) / simt::kBwdRows) * p.B;
   if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
   if (gkv > 0) {
-    simt::dkdv_kernel<T, DM><<<static_cast<unsigned>(gkv), simt::kBwdRows, smkv, st>>>(p);
+    simt::dkdv_kernel<T, DM><<<static_cast<unsigned>(gkv), simt::kBwdRows * simt::dkdv_split<DM>(), smkv, st>>>(p);
     ++*launches;
     if (int r = launch_result()) return r;
   }
