@@ -1,0 +1,63 @@
+"""Parity at the benchmark sizes (needs a B200).
+
+The C oracle is too slow at S = 8192, so full-size runs are checked against a
+dense float32 torch restatement of the same math on a sample of batch rows:
+softmax(scale·QKᵀ) with the reference's causal rule, its dropout mask (taken
+from the device RNG dump, which test_gpu_parity.py pins bit-for-bit to the
+oracle), stats = max + ln(l + 1e-6), and the exact backward.  fp16 tolerance
+as everywhere: max|new − ref| ≤ 2e-3 · max|ref|.
+"""
+import importlib
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+fa = importlib.import_module("tf-custom-flash-attention_b200")
+
+
+def dense_row(q, k, v, do, keep, scale, p, causal):
+    """float32 fwd + bwd of one batch row (2-D tensors)."""
+    q, k, v, do = (x.float() for x in (q, k, v, do))
+    s = (q @ k.T) * scale
+    if causal:
+        s = s.masked_fill(torch.triu(torch.ones_like(s, dtype=torch.bool), 1), float("-inf"))
+    m = s.amax(-1, keepdim=True)
+    e = torch.exp(s - m)
+    l = e.sum(-1, keepdim=True)
+    P = e / l
+    inv = 1.0 / (1.0 - p) if p > 1e-6 else 1.0
+    Pt = P * keep * inv
+    o = Pt @ v
+    stats = (m + torch.log(l + 1e-6)).squeeze(-1)
+    dv = Pt.T @ do
+    dP = (do @ v.T) * keep * inv
+    delta = (do * o).sum(-1, keepdim=True)
+    dS = P * (dP - delta) * scale
+    return o, stats, dS @ k, dS.T @ q, dv
+
+
+def rel(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max())
+
+
+@pytest.mark.parametrize("B,S,D,causal,p,rows", [
+    (4, 8192, 128, True, 0.1, (0, 3)),     # BASELINE configs[3] shape (batch reduced)
+    (8, 2048, 128, False, 0.0, (1, 6)),    # configs[2] shape
+    (8, 1024, 64, True, 0.0, (2, 7)),      # configs[1] shape
+])
+def test_full_size_against_dense(B, S, D, causal, p, rows):
+    g = torch.Generator(device="cuda").manual_seed(S + D)
+    q, k, v, do = (torch.randn(B, S, D, generator=g, device="cuda").half() for _ in range(4))
+    scale = D ** -0.5
+    o, s = fa.sdpa(q, k, v, 7, 0, scale=scale, dropout=p, causal_mask=causal)
+    dq, dk, dv = fa.sdpa_grad(q, k, v, o, s, do, 7, 0, dropout=p, scale=scale, causal_mask=causal)
+    for b in rows:
+        keep = 1.0 - fa.dropout_mask(7, fa.sharding.shard_offset(0, b, S, S), 1, S, S, p)[0].float()
+        ref = dense_row(q[b], k[b], v[b], do[b], keep, scale, p, causal)
+        for name, a, r in zip(("o", "stats", "dq", "dk", "dv"), (o[b], s[b], dq[b], dk[b], dv[b]), ref):
+            assert rel(a, r) <= 2e-3, (name, b, rel(a, r))
+        del keep, ref
+    torch.cuda.synchronize()

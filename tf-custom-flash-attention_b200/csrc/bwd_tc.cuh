@@ -267,21 +267,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
     const int64_t jw0 = n0 + (warp & 3) * 32;  // first key row of this warp
     const uint64_t step_i = static_cast<uint64_t>(p.S_kv) * kLcgA;  // counter step between query rows
-    auto row_val = [&](int t) -> float {      // this thread's share of tile t's row vectors
+    // Row vectors of tile t (thread e < 128 owns one value): the global load
+    // is issued a tile ahead and only consumed when stored to shared memory,
+    // so its latency overlaps the current tile's work.
+    const int which = e >> 6;  // 0: lse (log2 units), 1: delta
+    auto row_load = [&](int t, bool& in_range) -> float {
       const int64_t i = static_cast<int64_t>(tile0 + t) * kBwdTile + (e & 63);
-      const int which = e >> 6;
-      if (which >= 2) return 0.0f;
-      if (i >= p.S_q) return which == 0 ? INFINITY : 0.0f;
-      return which == 0 ? p.lse[b * p.S_q + i] * kLog2e : p.delta[b * p.S_q + i];
+      in_range = which < 2 && i < p.S_q;
+      if (!in_range) return 0.0f;
+      return which == 0 ? p.lse[b * p.S_q + i] : p.delta[b * p.S_q + i];
     };
-    float pre = nq > 0 ? row_val(0) : 0.0f;
+    bool pre_ok = false;
+    float pre = nq > 0 ? row_load(0, pre_ok) : 0.0f;
     bool ok = true;
     for (int t = 0; t < nq; ++t) {
       const int sb = t & 1;
       float* vb = vec + sb * 2 * kBwdTile;
-      if (e < 2 * kBwdTile) vb[e] = pre;
+      if (e < 2 * kBwdTile) vb[e] = which == 0 ? (pre_ok ? pre * kLog2e : INFINITY) : (pre_ok ? pre : 0.0f);
       mbar_arrive(&bars->vec_ready[sb]);
-      if (t + 1 < nq) pre = row_val(t + 1);
+      if (t + 1 < nq) pre = row_load(t + 1, pre_ok);
       if (!warp_wait(&bars->vec_ready[sb], (t >> 1) & 1, ctl) || !warp_wait(&bars->s_full[sb], (t >> 1) & 1, ctl)) {
         ok = false;
         break;
