@@ -67,6 +67,15 @@ int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const 
                   int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Backward that also propagates a gradient d_stats [B,S_q] (float32, device)
+ * reaching the stats output: stats is the row log-sum-exp, so it adds
+ * d_stats_i * p_ij to dS_ij.  No counterpart in the reference (its gradient
+ * registration drops it, mha.py:10-21); d_stats = NULL equals sdpa_b200_bwd. */
+int sdpa_b200_bwd_dstats(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                         const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q,
+                         int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal, uint64_t seed,
+                         uint64_t offset, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Writes mask[b][i][j] = 1 where (b,i,j) is dropped, from the same device RNG
  * routine the kernels use (diagnostic; no reference counterpart beyond the
  * RNG of sdpa/sdpa_utils.cuh:13-19).  mask is a device uint8 [B,S_q,S_kv]. */

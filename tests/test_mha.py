@@ -65,3 +65,28 @@ def test_mha_matches_dense_torch(layout):
     assert float((out.detach().float() - ref_out.detach()).abs().max() / ref_out.detach().abs().max()) < 2e-3
     for a, r in ((q.grad, qs.grad), (k.grad, ks.grad), (v.grad, vs.grad)):
         assert float((a.float() - r).abs().max() / r.abs().max()) < 5e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("p", [0.0, 0.2])
+def test_stats_gradient_extension(p):
+    """d(loss on stats and o)/d(q,k,v) with differentiable_stats=True vs dense float64 autograd."""
+    from oracle import dense
+
+    torch.manual_seed(1)
+    B, S, D = 2, 128, 64
+    q, k, v = (torch.randn(B, S, D, device="cuda").half().requires_grad_() for _ in range(3))
+    w = torch.randn(B, S, device="cuda")
+    o, s = fa.autograd.sdpa_with_stats(q, k, v, 3, 4, p, 0.125, True, differentiable_stats=True)
+    (o.float().sum() + (s * w).sum()).backward()
+    keep = torch.from_numpy(dense.keep_mask(3, 4, B, S, S, p)).cuda()
+    qd, kd, vd = (x.detach().double().requires_grad_() for x in (q, k, v))
+    sc = (qd @ kd.transpose(1, 2)) * 0.125
+    sc = sc.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device="cuda"), 1), float("-inf"))
+    P = sc.softmax(-1)
+    inv = 1 / (1 - p) if p > 1e-6 else 1.0
+    od = (P * keep * inv) @ vd
+    sd = torch.logsumexp(sc, -1)
+    (od.sum() + (sd * w.double()).sum()).backward()
+    for a, r in ((q.grad, qd.grad), (k.grad, kd.grad), (v.grad, vd.grad)):
+        assert float((a.double() - r).abs().max() / r.abs().max()) < 5e-3

@@ -34,6 +34,9 @@ def lib() -> ctypes.CDLL:
     L.sdpa_b200_bwd.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32, ci, u64,
                                 u64, vp, sz, vp]
     L.sdpa_b200_bwd.restype = ci
+    L.sdpa_b200_bwd_dstats.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32,
+                                       ci, u64, u64, vp, sz, vp]
+    L.sdpa_b200_bwd_dstats.restype = ci
     L.sdpa_b200_bwd_noalloc.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32,
                                         ci, u64, u64, vp]
     L.sdpa_b200_bwd_noalloc.restype = ci
@@ -64,5 +67,5 @@ EXPORTS = (
     "sdpa_b200_fwd", "sdpa_b200_bwd_workspace_bytes", "sdpa_b200_bwd", "sdpa_b200_dropout_mask",
     "sdpa_b200_strerror", "sdpa_b200_device_status", "sdpa_b200_set_wait_timeout_ns",
     "sdpa_b200_test_wait_timeout", "sdpa_b200_path", "sdpa_b200_last_launch_count", "sdpa_b200_version",
-    "sdpa_b200_bwd_noalloc",
+    "sdpa_b200_bwd_noalloc", "sdpa_b200_bwd_dstats",
 )

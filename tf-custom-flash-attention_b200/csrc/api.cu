@@ -144,8 +144,8 @@ size_t sdpa_b200_bwd_workspace_bytes(int, int64_t B, int64_t S_q, int64_t, int64
   return static_cast<size_t>(B) * static_cast<size_t>(S_q) * sizeof(float);
 }
 
-int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
-                  const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
+static int bwd_impl(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                    const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
                   int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
                   void* workspace, size_t workspace_bytes, void* stream) {
   t_launches = 0;
@@ -167,10 +167,27 @@ int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const 
   p.dk = dk;
   p.dv = dv;
   p.delta = static_cast<float*>(workspace);
+  p.d_stats = d_stats;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
   return dtype == SDPA_B200_F16 ? launch_bwd_simt_f16(p, st, &t_launches) : launch_bwd_simt_f32(p, st, &t_launches);
+}
+
+int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                  const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
+                  int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  return bwd_impl(dtype, q, k, v, out, stats, nullptr, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,
+                  causal, seed, offset, workspace, workspace_bytes, stream);
+}
+
+int sdpa_b200_bwd_dstats(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                         const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q,
+                         int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal, uint64_t seed,
+                         uint64_t offset, void* workspace, size_t workspace_bytes, void* stream) {
+  return bwd_impl(dtype, q, k, v, out, stats, d_stats, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,
+                  causal, seed, offset, workspace, workspace_bytes, stream);
 }
 
 int sdpa_b200_dropout_mask(uint64_t seed, uint64_t offset, int64_t B, int64_t S_q, int64_t S_kv, float dropout,

@@ -18,7 +18,8 @@ struct Params {
   const void* o;        // backward: forward output
   const void* d_o;      // backward: gradient of the output
   const float* lse;     // backward: stats of the forward (natural log)
-  float* delta;         // backward workspace: rowsum(dO*O), [B*S_q]
+  float* delta;         // backward workspace: rowsum(dO*O) - d_stats, [B*S_q]
+  const float* d_stats; // backward: gradient reaching stats (nullptr = none)
   // outputs
   void* out;
   float* stats;

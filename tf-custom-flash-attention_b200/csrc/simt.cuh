@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
     if (d < p.D_v) O[d] = from_f<T>(acc[d] * inv);
 }
 
-// D_i = sum_d dO[i,d] * O[i,d] (fp32), one warp per row.
+// D_i = sum_d dO[i,d] * O[i,d] (fp32), one warp per row (minus the stats gradient, if any).
 template <typename T>
 __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
@@ -110,7 +110,9 @@ __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   for (int d = lane; d < p.D_v; d += 32) s = fmaf(to_f<T>(dO[d]), to_f<T>(O[d]), s);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) p.delta[row] = s;
+  // A gradient g_i reaching stats_i = logsumexp adds g_i * p_ij to dS_ij,
+  // i.e. it enters dS = p (dP - D) as D - g.
+  if (lane == 0) p.delta[row] = p.d_stats ? s - p.d_stats[row] : s;
 }
 
 // Gradient of one score element.  Returns false when skipped (p <= 1e-6,

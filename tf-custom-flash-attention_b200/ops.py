@@ -103,8 +103,11 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seed, offset, scale:
 
 
 def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale: float = 1.0,
-              causal_mask: bool = False):
-    """The ``SdpaGrad`` op: returns (dq, dk, dv) shaped like (q, k, v)."""
+              causal_mask: bool = False, *, d_stats=None):
+    """The ``SdpaGrad`` op: returns (dq, dk, dv) shaped like (q, k, v).
+
+    ``d_stats`` (extension, not in the reference): a float32 [B, S_q] gradient
+    reaching ``stats``; it is propagated as the log-sum-exp it is."""
     for i, t in enumerate((q, k, v)):
         _rank3(t, i)
     seed_v = _scalar_u64(seed, "seed")
@@ -140,10 +143,20 @@ def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale
     ws = torch.empty((max(ws_bytes, 4) + 3) // 4, dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
         st = torch.cuda.current_stream().cuda_stream
-        rc = L.sdpa_b200_bwd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), stats.data_ptr(),
-                             do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
-                             float(scale), float(dropout), int(bool(causal_mask)), seed_v, offset_v,
-                             ws.data_ptr(), ws_bytes, st)
+        if d_stats is None:
+            rc = L.sdpa_b200_bwd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), stats.data_ptr(),
+                                 do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
+                                 float(scale), float(dropout), int(bool(causal_mask)), seed_v, offset_v,
+                                 ws.data_ptr(), ws_bytes, st)
+        else:
+            d_stats = d_stats.to(torch.float32).contiguous()
+            if tuple(d_stats.shape) != (B, S_q):
+                raise InvalidArgumentError("d_stats must be [B, S_q]")
+            rc = L.sdpa_b200_bwd_dstats(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                        stats.data_ptr(), d_stats.data_ptr(), do.data_ptr(), dq.data_ptr(),
+                                        dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v, float(scale),
+                                        float(dropout), int(bool(causal_mask)), seed_v, offset_v, ws.data_ptr(),
+                                        ws_bytes, st)
     _check(rc)
     return dq, dk, dv
 
