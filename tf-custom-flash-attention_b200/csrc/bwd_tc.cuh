@@ -263,10 +263,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int64_t j = n0 + r;                 // key row
     float* vec = reinterpret_cast<float*>(smem + Cfg::kVecOff);  // [2][2][64]
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
-    const bool all_drop = p.drop_thr > 0xffffffffull;
-    const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
+    const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
     const int64_t jw0 = n0 + (warp & 3) * 32;  // first key row of this warp
     const uint64_t step_i = static_cast<uint64_t>(p.S_kv) * kLcgA;  // counter step between query rows
+    const uint32_t step_lo = static_cast<uint32_t>(step_i), step_hi = static_cast<uint32_t>(step_i >> 32);
     // Row vectors of tile t (thread e < 128 owns one value): the global load
     // is issued a tile ahead and only consumed when stored to shared memory,
     // so its latency overlaps the current tile's work.
@@ -302,10 +302,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int64_t d = j - i0;
         lo = static_cast<int>(d < -1 ? -1 : (d > 32 ? 32 : d));
       }
-      uint64_t st = 0;
-      if (DROP)
-        st = lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i0) * static_cast<uint64_t>(p.S_kv),
-                       static_cast<uint64_t>(j));
+      LcgWalk st(DROP ? lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + i0) *
+                                                static_cast<uint64_t>(p.S_kv),
+                                  static_cast<uint64_t>(j))
+                      : 0);
       uint32_t pk[16], dk[16];
 #pragma unroll
       for (int c4 = 0; c4 < 8; ++c4) {
@@ -322,8 +322,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           // dropped: P~ = 0, dS = -p D; kept: P~ = p/(1-r), dS = P~ (dP - D (1-r)) = p (dP/(1-r) - D)
           float kf = 1.0f;
           if (DROP) {
-            const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-            st += step_i;
+            const bool dr = st.dropped(thr_m1);
+            st.step(step_lo, step_hi);
             kf = dr ? 0.0f : dp_inv;
           }
           ptv[e] = pr * kf;
@@ -432,8 +432,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
     const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
-    const bool all_drop = p.drop_thr > 0xffffffffull;
-    const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
+    const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
     const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv);
     bool ok = true;
     for (int t = 0; t < nkv; ++t) {
@@ -451,7 +450,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int64_t lim64 = p.S_kv - j0;
       if (p.causal) lim64 = min(lim64, i - j0 + 1);
       const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
-      uint64_t st = DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0;
+      LcgWalk st(DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0);
       uint32_t dk[16];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
@@ -463,8 +462,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const float dpc = __uint_as_float(dpv[c + e]);
           float kf = 1.0f;  // see the dK/dV kernel: dS = p (kf dP - D)
           if (DROP) {
-            const bool dr = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-            st += kLcgA;
+            const bool dr = st.dropped(thr_m1);
+            st.step();
             kf = dr ? 0.0f : dp_inv;
           }
           dsv[e] = pr * fmaf(kf, dpc, -delta);

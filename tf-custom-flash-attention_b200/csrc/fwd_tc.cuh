@@ -282,18 +282,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       float rs = 0.0f;
       uint32_t pk[64];
       if (DROP) {
-        uint64_t st = lcg_state(rbase, static_cast<uint64_t>(kv0));
-        const bool all_drop = p.drop_thr > 0xffffffffull;
-        const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
+        LcgWalk st(lcg_state(rbase, static_cast<uint64_t>(kv0)));
+        const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
           float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
           float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
           rs += p0 + p1;
-          const bool d0 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-          st += kLcgA;
-          const bool d1 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-          st += kLcgA;
+          const bool d0 = st.dropped(thr_m1);
+          st.step();
+          const bool d1 = st.dropped(thr_m1);
+          st.step();
           pk[c / 2] = pack_half2(d0 ? 0.0f : p0, d1 ? 0.0f : p1);
         }
       } else {
@@ -581,8 +580,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + row) * static_cast<uint64_t>(p.S_kv);
     const bool fold = p.scale_log2 > 0.0f;  // scale folded into one FFMA (max over raw scores)
     const float sl = fold ? p.scale_log2 : 1.0f;
-    const bool all_drop = p.drop_thr > 0xffffffffull;
-    const uint32_t thr32 = all_drop ? 0xffffffffu : static_cast<uint32_t>(p.drop_thr);
+    const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
     float m_run = -INFINITY;  // true running max (log2 units, scaled)
     float m_use = -INFINITY;  // reference max the exponentials are taken against
     float l = 0.0f;           // sum of exp2(x - m_use), pre-dropout
@@ -629,16 +627,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       float rs = 0.0f;
       // P packed in place: r[c/2] <- (p_c, p_c+1) once both are read
       if (DROP) {
-        uint64_t st = lcg_state(rbase, static_cast<uint64_t>(kv0));
+        LcgWalk st(lcg_state(rbase, static_cast<uint64_t>(kv0)));
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
           const float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
           const float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
           rs += p0 + p1;
-          const bool d0 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-          st += kLcgA;
-          const bool d1 = all_drop || static_cast<uint32_t>(st >> 32) < thr32;
-          st += kLcgA;
+          const bool d0 = st.dropped(thr_m1);
+          st.step();
+          const bool d1 = st.dropped(thr_m1);
+          st.step();
           r[c / 2] = pack_half2(d0 ? 0.0f : p0, d1 ? 0.0f : p1);
         }
       } else {

@@ -225,4 +225,24 @@ constexpr uint64_t kLcgC = 1442695040888963407ULL;
 __device__ __forceinline__ uint64_t lcg_state(uint64_t base, uint64_t j) { return (base + j) * kLcgA + kLcgC; }
 __device__ __forceinline__ bool dropped(uint64_t state, uint64_t thr) { return (state >> 32) < thr; }
 
+// The same walk on the two 32-bit halves of the state: one step adds A with a
+// carry from the low word (2 instructions); the drop test reads the high word.
+struct LcgWalk {
+  uint32_t lo, hi;
+  __device__ __forceinline__ explicit LcgWalk(uint64_t s)
+      : lo(static_cast<uint32_t>(s)), hi(static_cast<uint32_t>(s >> 32)) {}
+  __device__ __forceinline__ void step() {
+    asm("add.cc.u32 %0, %0, %2;\n\taddc.u32 %1, %1, %3;"
+        : "+r"(lo), "+r"(hi)
+        : "n"(static_cast<uint32_t>(kLcgA & 0xffffffffu)), "n"(static_cast<uint32_t>(kLcgA >> 32)));
+  }
+  __device__ __forceinline__ void step(uint32_t inc_lo, uint32_t inc_hi) {
+    asm("add.cc.u32 %0, %0, %2;\n\taddc.u32 %1, %1, %3;" : "+r"(lo), "+r"(hi) : "r"(inc_lo), "r"(inc_hi));
+  }
+  // dropped iff hi32(state) < thr, tested as hi <= thr - 1 (thr in [1, 2^32]),
+  // so rate >= 1 (thr = 2^32) needs no separate case
+  __device__ __forceinline__ bool dropped(uint32_t thr_m1) const { return hi <= thr_m1; }
+};
+__host__ __device__ inline uint32_t drop_thr_m1(uint64_t thr) { return static_cast<uint32_t>(thr - 1); }
+
 }  // namespace sdpa_b200
