@@ -191,6 +191,68 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, int nchunks, int c
   }
 }
 
+// Elementwise pass of the dK/dV kernel over 32 columns (query rows) of one key
+// row: P~^T and the unscaled dS^T as packed fp16 pairs.  MASK: some columns
+// fail the causal test c >= lo (only warps on the diagonal).
+template <bool DROP, bool MASK>
+__device__ __forceinline__ void dkdv_elems(const uint32_t* sv, const uint32_t* dpv, const float* vbc, int lo,
+                                           float sl2, float dp_inv, LcgWalk& st, uint32_t thr_m1, uint32_t step_lo,
+                                           uint32_t step_hi, uint32_t* pk, uint32_t* dk) {
+#pragma unroll
+  for (int c4 = 0; c4 < 8; ++c4) {
+    const float4 L4 = *reinterpret_cast<const float4*>(vbc + 4 * c4);
+    const float4 D4 = *reinterpret_cast<const float4*>(vbc + kBwdTile + 4 * c4);
+    const float Lv[4] = {L4.x, L4.y, L4.z, L4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w};
+    float ptv[4], dsv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = 4 * c4 + e;
+      float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -Lv[e]));
+      // skip rule of sdpa/sdpa_bwd.cu.cc:131, causal mask
+      pr = (pr > kEps && (!MASK || c >= lo)) ? pr : 0.0f;
+      const float dpc = __uint_as_float(dpv[c]);
+      // dropped: P~ = 0, dS = -p D; kept: P~ = p/(1-r), dS = P~ (dP - D (1-r)) = p (dP/(1-r) - D)
+      float kf = 1.0f;
+      if (DROP) {
+        const bool dr = st.dropped(thr_m1);
+        st.step(step_lo, step_hi);
+        kf = dr ? 0.0f : dp_inv;
+      }
+      ptv[e] = pr * kf;
+      dsv[e] = pr * fmaf(kf, dpc, -Dv[e]);
+    }
+    pk[2 * c4] = pack_half2(ptv[0], ptv[1]);
+    pk[2 * c4 + 1] = pack_half2(ptv[2], ptv[3]);
+    dk[2 * c4] = pack_half2(dsv[0], dsv[1]);
+    dk[2 * c4 + 1] = pack_half2(dsv[2], dsv[3]);
+  }
+}
+
+// Elementwise pass of the dQ kernel over 32 columns (keys) of one query row:
+// the unscaled dS as packed fp16 pairs.  MASK: some columns fail c < lim.
+template <bool DROP, bool MASK>
+__device__ __forceinline__ void dq_elems(const uint32_t* sv, const uint32_t* dpv, int lim, float sl2, float lse2,
+                                         float delta, float dp_inv, LcgWalk& st, uint32_t thr_m1, uint32_t* dk) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float dsv[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float pr = ex2(fmaf(__uint_as_float(sv[c + e]), sl2, -lse2));
+      pr = (pr > kEps && (!MASK || c + e < lim)) ? pr : 0.0f;  // skip rule, key range, causal mask
+      const float dpc = __uint_as_float(dpv[c + e]);
+      float kf = 1.0f;  // see dkdv_elems: dS = p (kf dP - D)
+      if (DROP) {
+        const bool dr = st.dropped(thr_m1);
+        st.step();
+        kf = dr ? 0.0f : dp_inv;
+      }
+      dsv[e] = pr * fmaf(kf, dpc, -delta);
+    }
+    dk[c / 2] = pack_half2(dsv[0], dsv[1]);
+  }
+}
+
 template <int DQK, int DV, bool DROP>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -297,8 +359,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_ld();
       const int64_t i0 = static_cast<int64_t>(tile0 + t) * kBwdTile + col0;
       // causal: column c is valid iff i0 + c >= j; only warps on the diagonal test it
+      const bool masked = p.causal && i0 < jw0 + 31;  // warp-uniform
       int lo = -1;
-      if (p.causal && i0 < jw0 + 31) {
+      if (masked) {
         const int64_t d = j - i0;
         lo = static_cast<int>(d < -1 ? -1 : (d > 32 ? 32 : d));
       }
@@ -307,33 +370,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                   static_cast<uint64_t>(j))
                       : 0);
       uint32_t pk[16], dk[16];
-#pragma unroll
-      for (int c4 = 0; c4 < 8; ++c4) {
-        const float4 L4 = *reinterpret_cast<const float4*>(vb + col0 + 4 * c4);
-        const float4 D4 = *reinterpret_cast<const float4*>(vb + kBwdTile + col0 + 4 * c4);
-        const float Lv[4] = {L4.x, L4.y, L4.z, L4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w};
-        float ptv[4], dsv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 4 * c4 + e;
-          float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -Lv[e]));
-          pr = (pr > kEps && c >= lo) ? pr : 0.0f;  // skip rule of sdpa/sdpa_bwd.cu.cc:131, causal mask
-          const float dpc = __uint_as_float(dpv[c]);
-          // dropped: P~ = 0, dS = -p D; kept: P~ = p/(1-r), dS = P~ (dP - D (1-r)) = p (dP/(1-r) - D)
-          float kf = 1.0f;
-          if (DROP) {
-            const bool dr = st.dropped(thr_m1);
-            st.step(step_lo, step_hi);
-            kf = dr ? 0.0f : dp_inv;
-          }
-          ptv[e] = pr * kf;
-          dsv[e] = pr * fmaf(kf, dpc, -Dv[e]);
-        }
-        pk[2 * c4] = pack_half2(ptv[0], ptv[1]);
-        pk[2 * c4 + 1] = pack_half2(ptv[2], ptv[3]);
-        dk[2 * c4] = pack_half2(dsv[0], dsv[1]);
-        dk[2 * c4 + 1] = pack_half2(dsv[2], dsv[3]);
-      }
+      if (masked)
+        dkdv_elems<DROP, true>(sv, dpv, vb + col0, lo, sl2, dp_inv, st, thr_m1, step_lo, step_hi, pk, dk);
+      else
+        dkdv_elems<DROP, false>(sv, dpv, vb + col0, lo, sl2, dp_inv, st, thr_m1, step_lo, step_hi, pk, dk);
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, pk);
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
       tmem_wait_st();
@@ -450,26 +490,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int64_t lim64 = p.S_kv - j0;
       if (p.causal) lim64 = min(lim64, i - j0 + 1);
       const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
+      // warp-uniform: does any row of this warp see a masked column in this slice?
+      const int64_t iw0 = m0 + (warp & 3) * 32;
+      const bool masked = (p.S_kv - j0 < 32) || (p.causal && iw0 - j0 + 1 < 32);
       LcgWalk st(DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0);
       uint32_t dk[16];
-#pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        float dsv[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float pr = ex2(fmaf(__uint_as_float(sv[c + e]), sl2, -lse2));
-          pr = (pr > kEps && c + e < lim) ? pr : 0.0f;  // skip rule, key range, causal mask
-          const float dpc = __uint_as_float(dpv[c + e]);
-          float kf = 1.0f;  // see the dK/dV kernel: dS = p (kf dP - D)
-          if (DROP) {
-            const bool dr = st.dropped(thr_m1);
-            st.step();
-            kf = dr ? 0.0f : dp_inv;
-          }
-          dsv[e] = pr * fmaf(kf, dpc, -delta);
-        }
-        dk[c / 2] = pack_half2(dsv[0], dsv[1]);
-      }
+      if (masked)
+        dq_elems<DROP, true>(sv, dpv, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk);
+      else
+        dq_elems<DROP, false>(sv, dpv, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk);
       SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
       tmem_wait_st();
       tc_fence_before();
