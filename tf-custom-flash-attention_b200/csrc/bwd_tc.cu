@@ -15,18 +15,17 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
   using Cfg = tc::BwdCfg<DQK, DV>;
   auto kkv = tc::dkdv_kernel<DQK, DV, DROP>;
-  auto kq = tc::dq_kernel<DQK, DV, DROP>;
+  auto kq = tc::dq2_kernel<DQK, DV, DROP>;
+  using QCfg = tc::Dq2Cfg<DQK, DV>;
   if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (ensure_smem(kq, Cfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
-  CUtensorMap k128, v128, q64, do64, q128, do128, k64, v64;
+  if (ensure_smem(kq, QCfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
+  CUtensorMap k128, v128, q64, do64, q128, do128;
   if (!make_map_f16(&k128, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdRows) ||
       !make_map_f16(&v128, p.v, p.B, p.S_kv, p.D_v, tc::kBwdRows) ||
       !make_map_f16(&q64, p.q, p.B, p.S_q, p.D_qk, tc::kBwdTile) ||
       !make_map_f16(&do64, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdTile) ||
       !make_map_f16(&q128, p.q, p.B, p.S_q, p.D_qk, tc::kBwdRows) ||
-      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows) ||
-      !make_map_f16(&k64, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdTile) ||
-      !make_map_f16(&v64, p.v, p.B, p.S_kv, p.D_v, tc::kBwdTile))
+      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows))
     return SDPA_B200_ECUDA;
   const int64_t rows = p.B * p.S_q;
   simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
@@ -38,7 +37,7 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   kkv<<<static_cast<unsigned>(gkv), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
   ++*launches;
   if (int r = launch_result()) return r;
-  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, Cfg::kSmemBytes, st>>>(q128, do128, k64, v64, p);
+  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
   ++*launches;
   return launch_result();
 }

@@ -10,8 +10,9 @@
 //     dV  += P~^T dO,  dK += dS^T Q             (TS MMA: A = P~ / dS read
 //                                                from TMEM, written over S^T / dP^T)
 //   dK is multiplied by `scale` in the epilogue.
-// dq_kernel: one CTA = 128 query rows; streams 64-row K/V tiles; S = Q K^T,
-//   dP = dO V^T, dS as above, dQ += dS K (TS MMA); dQ *= scale at the end.
+// dq2_kernel: one CTA = 128 query rows; streams 128-row K/V tiles; S = Q K^T,
+//   dP = dO V^T, dS as above, dQ += dS K (TS MMA); dQ *= scale at the end
+//   (layout and pipeline at its definition below).
 //
 // Roles (320 threads): warps 0-7 elementwise (warp w serves TMEM lanes
 // 32*(w%4).. and column half w/4 of each 64-column tile), warp 8 TMA
@@ -401,23 +402,81 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ============================================================================
+// dQ kernel with 128-key tiles.  One CTA = 128 query rows; per key tile t:
+//     S = Q K_t^T, dP = dO V_t^T      (SS MMA, N = 128: full rate)
+//     dS = p (kf dP - D)               (8 elementwise warps, 64 columns each)
+//     dQ += dS K_t                     (TS MMA, A = dS from its own TMEM buffer)
+// The elementwise warps release S/dP as soon as they have loaded them, so the
+// MMAs of tile t+1 run while dS of tile t is computed.  TMEM: dQ [0,128),
+// dS [128,192) (fp16 pairs), S [256,384), dP [384,512).  K is held until dQ
+// consumed it (3-stage ring), V only until dP (2 stages); Q and dO resident.
+template <int DQK, int DV>
+struct Dq2Cfg {
+  static constexpr int kKStages = 3, kVStages = 2;
+  static constexpr uint32_t kQBytes = kBwdRows * DQK * 2, kOBytes = kBwdRows * DV * 2;
+  static constexpr uint32_t kKBytes = kBwdRows * DQK * 2, kVBytes = kBwdRows * DV * 2;
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kOOff = kQOff + kQBytes;
+  static constexpr uint32_t kKOff = kOOff + kOBytes;
+  static constexpr uint32_t kVOff = kKOff + kKStages * kKBytes;
+  static constexpr uint32_t kBarOff = kVOff + kVStages * kVBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kDQ = 0, kDS = 128, kS = 256, kDP = 384;
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+struct Dq2Barriers {
+  uint64_t res_full;
+  uint64_t k_full[3], k_empty[3];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full, sdp_free, ds_full, ds_empty;
+  uint64_t acc_done, mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
 template <int DQK, int DV, bool DROP>
 __global__ void __launch_bounds__(kBwdThreads, 1)
-    dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-              const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
-  using Cfg = BwdCfg<DQK, DV>;
+    dq2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using Cfg = Dq2Cfg<DQK, DV>;
+  constexpr int TN = kBwdRows;  // keys per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + Cfg::kBarOff);
+  Dq2Barriers* bars = reinterpret_cast<Dq2Barriers*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int64_t n_qt = (p.S_q + kBwdRows - 1) / kBwdRows;
   const int64_t b = blockIdx.x % p.B;
   const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
   const int64_t m0 = qt * kBwdRows;
-  const int64_t n_kv_all = (p.S_kv + kBwdTile - 1) / kBwdTile;
-  const int nkv = static_cast<int>(p.causal ? min(n_kv_all, (m0 + kBwdRows - 1) / kBwdTile + 1) : n_kv_all);
+  const int64_t n_kv_all = (p.S_kv + TN - 1) / TN;
+  const int nkv = static_cast<int>(p.causal ? min(n_kv_all, qt + 1) : n_kv_all);
 
-  bwd_setup(bars, Cfg::kTmemCols, warp);
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->res_full, 1);
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->sdp_free, 256);
+    mbar_init(&bars->ds_full, 256);
+    mbar_init(&bars->ds_empty, 1);
+    mbar_init(&bars->acc_done, 1);
+    mbar_init(&bars->mma_done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   WaitCtl ctl;
   ctl.deadline_ns = globaltimer_ns() + p.timeout_ns;
@@ -425,34 +484,89 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 8) {
-    if (lane == 0 && nkv > 0)
-      bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_q, &tm_do, &tm_k, &tm_v, static_cast<int>(m0), 0, nkv,
-                                 static_cast<int>(b), ctl, p.timeout_ns);
-  } else if (warp == 9) {
+    // ------------------------------------------------------ TMA producer
     if (lane == 0 && nkv > 0) {
-      bool ok = mbar_wait(&bars->res_full, 0, ctl);
-      auto grads = [&](int t) -> bool {
-        const int s = t % kBwdStages, sb = t & 1;
-        if (!mbar_wait(&bars->p_full[sb], (t >> 1) & 1, ctl)) return false;
+      mbar_expect_tx(&bars->res_full, Cfg::kQBytes + Cfg::kOBytes);
+#pragma unroll
+      for (int c = 0; c < DQK / 64; ++c)
+        tma_load_3d(smem + Cfg::kQOff + c * kBwdRows * 128, &tm_q, c * 64, static_cast<int>(m0), static_cast<int>(b),
+                    &bars->res_full);
+#pragma unroll
+      for (int c = 0; c < DV / 64; ++c)
+        tma_load_3d(smem + Cfg::kOOff + c * kBwdRows * 128, &tm_do, c * 64, static_cast<int>(m0),
+                    static_cast<int>(b), &bars->res_full);
+      int issued = 0;
+      for (int t = 0; t < nkv; ++t) {
+        const int ks = t % 3, vs = t & 1;
+        if (!mbar_wait(&bars->k_empty[ks], ((t / 3) & 1) ^ 1, ctl)) break;
+        mbar_expect_tx(&bars->k_full[ks], Cfg::kKBytes);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + Cfg::kKOff + ks * Cfg::kKBytes + c * TN * 128, &tm_k, c * 64, t * TN,
+                      static_cast<int>(b), &bars->k_full[ks]);
+        if (!mbar_wait(&bars->v_empty[vs], ((t >> 1) & 1) ^ 1, ctl)) break;
+        mbar_expect_tx(&bars->v_full[vs], Cfg::kVBytes);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(smem + Cfg::kVOff + vs * Cfg::kVBytes + c * TN * 128, &tm_v, c * 64, t * TN,
+                      static_cast<int>(b), &bars->v_full[vs]);
+        issued = t + 1;
+      }
+      if (*ctl.abort_flag) {  // let copies in flight land before the CTA exits
+        WaitCtl drain = ctl;
+        drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+        int dummy = 0;
+        drain.abort_flag = &dummy;
+        mbar_wait(&bars->res_full, 0, drain);
+        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) {
+          mbar_wait(&bars->k_full[t % 3], (t / 3) & 1, drain);
+          mbar_wait(&bars->v_full[t & 1], (t >> 1) & 1, drain);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t idesc_s = make_idesc(kBwdRows, TN, false, false, false);
+      constexpr uint32_t idesc_dq = make_idesc(kBwdRows, DQK, false, true, false);
+      auto issue_scores = [&](int t) -> bool {
+        const int ks = t % 3, vs = t & 1;
+        if (!mbar_wait(&bars->k_full[ks], (t / 3) & 1, ctl)) return false;
+        if (!mbar_wait(&bars->v_full[vs], (t >> 1) & 1, ctl)) return false;
         tc_fence_after();
-        // dQ += dS K_t
-        bwd_issue_acc<DQK>(tmem + Cfg::kAcc0, tmem + Cfg::kDP + sb * kBwdTile, sbase + Cfg::kStAOff + s * Cfg::kStA,
-                           t == 0);
-        mma_commit(&bars->st_empty[s]);
+        const uint32_t kb = sbase + Cfg::kKOff + ks * Cfg::kKBytes, vb = sbase + Cfg::kVOff + vs * Cfg::kVBytes;
+        const uint32_t qb = sbase + Cfg::kQOff, ob = sbase + Cfg::kOOff;
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32;
+          mma_f16_ss(tmem + Cfg::kS, make_sw128_desc(qb + off, 16, 1024), make_sw128_desc(kb + off, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32;
+          mma_f16_ss(tmem + Cfg::kDP, make_sw128_desc(ob + off, 16, 1024), make_sw128_desc(vb + off, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&bars->v_empty[vs]);  // V_t is no longer read
+        mma_commit(&bars->s_full);
         return true;
       };
+      bool ok = mbar_wait(&bars->res_full, 0, ctl) && issue_scores(0);
       for (int t = 0; ok && t < nkv; ++t) {
-        const int s = t % kBwdStages, sb = t & 1;
-        if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl)) {
-          ok = false;
-          break;
-        }
+        // S/dP of tile t are in registers of the elementwise warps: start tile t+1
+        if (!mbar_wait(&bars->sdp_free, t & 1, ctl)) { ok = false; break; }
+        if (t + 1 < nkv && !issue_scores(t + 1)) { ok = false; break; }
+        if (!mbar_wait(&bars->ds_full, t & 1, ctl)) { ok = false; break; }
         tc_fence_after();
-        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S = Q K^T, dP = dO V^T
-        mma_commit(&bars->s_full[sb]);
-        if (t > 0 && !grads(t - 1)) ok = false;
+        const uint32_t kb = sbase + Cfg::kKOff + (t % 3) * Cfg::kKBytes;
+#pragma unroll
+        for (int kk = 0; kk < TN / 16; ++kk)
+          mma_f16_ts(tmem + Cfg::kDQ, tmem + Cfg::kDS + kk * 8, make_sw128_desc(kb + kk * 16 * 128, TN * 128, 1024),
+                     idesc_dq, (t > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars->k_empty[t % 3]);
+        mma_commit(&bars->ds_empty);
       }
-      if (ok) ok = grads(nkv - 1);
       mma_commit(&bars->acc_done);
       mma_commit(&bars->mma_done);
       WaitCtl drain = ctl;
@@ -463,11 +577,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     // ------------------------------------------------ elementwise warps
-    const int half = warp >> 2;
+    const int half = warp >> 2;            // 64-column half of each 128-key tile
     const int r = (warp & 3) * 32 + lane;  // TMEM lane = query row in tile
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const int col0 = half * 32;
+    const int col0 = half * 64;
     const int64_t i = m0 + r;
+    const int64_t iw0 = m0 + (warp & 3) * 32;
     const bool row_ok = i < p.S_q;
     const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
     const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
@@ -476,39 +591,51 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv);
     bool ok = true;
     for (int t = 0; t < nkv; ++t) {
-      const int sb = t & 1;
-      if (!warp_wait(&bars->s_full[sb], (t >> 1) & 1, ctl)) {
+      if (!warp_wait(&bars->s_full, t & 1, ctl)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[32], dpv[32];
-      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kS + sb * kBwdTile + col0, sv);
-      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dpv);
+      uint32_t sv[64], dpv[64];
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kS + col0, sv);
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kS + col0 + 32, (sv + 32));
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + col0, dpv);
+      SDPA_TMEM_LD32(tmem + lane_base + Cfg::kDP + col0 + 32, (dpv + 32));
       tmem_wait_ld();
-      const int64_t j0 = static_cast<int64_t>(t) * kBwdTile + col0;
-      int64_t lim64 = p.S_kv - j0;
-      if (p.causal) lim64 = min(lim64, i - j0 + 1);
-      const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
-      // warp-uniform: does any row of this warp see a masked column in this slice?
-      const int64_t iw0 = m0 + (warp & 3) * 32;
-      const bool masked = (p.S_kv - j0 < 32) || (p.causal && iw0 - j0 + 1 < 32);
-      LcgWalk st(DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0);
-      uint32_t dk[16];
-      if (masked)
-        dq_elems<DROP, true>(sv, dpv, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk);
-      else
-        dq_elems<DROP, false>(sv, dpv, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk);
-      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDP + sb * kBwdTile + col0, dk);
+      tc_fence_before();
+      mbar_arrive(&bars->sdp_free);  // S/dP may be overwritten by the next tile's MMAs
+      uint32_t dk[32];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int64_t j0 = static_cast<int64_t>(t) * TN + col0 + 32 * h2;
+        int64_t lim64 = p.S_kv - j0;
+        if (p.causal) lim64 = min(lim64, i - j0 + 1);
+        const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > 32 ? 32 : lim64));
+        const bool masked = (p.S_kv - j0 < 32) || (p.causal && iw0 - j0 + 1 < 32);  // warp-uniform
+        LcgWalk st(DROP ? lcg_state(rbase, static_cast<uint64_t>(j0)) : 0);
+        if (masked)
+          dq_elems<DROP, true>(sv + 32 * h2, dpv + 32 * h2, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk + 16 * h2);
+        else
+          dq_elems<DROP, false>(sv + 32 * h2, dpv + 32 * h2, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk + 16 * h2);
+      }
+      if (t > 0) {  // dQ of the previous tile must have read the dS buffer
+        if (!warp_wait(&bars->ds_empty, (t - 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + half * 32, dk);
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + half * 32 + 16, (dk + 16));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[sb]);
+      mbar_arrive(&bars->ds_full);
     }
     if (ok && nkv > 0) ok = warp_wait(&bars->acc_done, 0, ctl);
     if (ok) {
       tc_fence_after();
       __half* dq_row = static_cast<__half*>(p.dq) + (b * p.S_q + i) * p.D_qk;
-      store_acc_row(tmem + lane_base + Cfg::kAcc0 + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nkv > 0,
+      store_acc_row(tmem + lane_base + Cfg::kDQ + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nkv > 0,
                     row_ok, dq_row, p.D_qk);
     }
   }
