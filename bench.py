@@ -21,6 +21,7 @@ reduced, see `cpu_sample`), in the same unit.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import os
@@ -214,13 +215,26 @@ def run_ours(args, w):
     stream = torch.cuda.current_stream()
 
     launches = [0]
+    # per-kernel timing of the backward (rowsum | dK/dV | dQ) on the launching
+    # stream, through the library's diagnostic event hook (tensor-core path only)
+    per_kernel = fa.kernel_path(dt, Dq, Dv, backward=True) == "tcgen05"
+    kev = []
 
     def step():
         o, s = fa.sdpa(q, k, v, w["seed"], offset, **kw)
         n = fa.last_launch_count()
         e_mid = torch.cuda.Event(enable_timing=True)
         e_mid.record(stream)
+        if per_kernel:
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            for e in evs:  # torch creates the CUDA event on its first record
+                e.record(stream)
+            arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
+            fa._lib.lib().sdpa_b200_set_bwd_events(arr, 4)
+            kev.append(evs)
         dq, dk, dv = fa.sdpa_grad(q, k, v, o, s, do, w["seed"], offset, **kw)
+        if per_kernel:
+            fa._lib.lib().sdpa_b200_set_bwd_events(None, 0)
         launches[0] += n + fa.last_launch_count()
         return e_mid
 
@@ -233,6 +247,7 @@ def run_ours(args, w):
     clocks = ClockSampler(local)
     clocks.start()
     launches[0] = 0
+    kev.clear()
     evs = []
     e0 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -247,6 +262,10 @@ def run_ours(args, w):
     total_ms = e0.elapsed_time(prev)
     fwd_ms = sum(a.elapsed_time(m) for a, m, _ in evs) / args.steps
     bwd_ms = sum(m.elapsed_time(e) for _, m, e in evs) / args.steps
+    kernel_ms = None
+    if per_kernel and len(kev) == args.steps:
+        kernel_ms = {name: sum(e[i].elapsed_time(e[i + 1]) for e in kev) / args.steps
+                     for i, name in enumerate(("delta", "dkdv", "dq"))}
     clk = clocks.stop()
     per_rank = [{"rank": rank, "ms_per_step": total_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
                  "reasons": clk.get("reasons")}]
@@ -304,11 +323,20 @@ def run_ours(args, w):
     peak, peak_kind = peaks()
     fwd_tf = f_fwd / (fwd_ms * 1e-3) / 1e12
     bwd_tf = f_bwd / (bwd_ms * 1e-3) / 1e12
-    dominant = ("bwd", bwd_tf, bwd_ms, f_bwd) if bwd_ms >= fwd_ms else ("fwd", fwd_tf, fwd_ms, f_fwd)
+    # Dominant kernel.  Algorithmic FLOPs per launch: fwd = the forward; of the
+    # backward's 5 MMA-units (S, dP, dV, dK, dQ), dK/dV carries 4 and dQ 1 (its
+    # S and dP are recomputation, not algorithmic work).
+    cands = [("fwd_pair_kernel", fwd_ms, f_fwd)]
+    if kernel_ms:
+        cands += [("dkdv_kernel", kernel_ms["dkdv"], 0.8 * f_bwd), ("dq2_kernel", kernel_ms["dq"], 0.2 * f_bwd)]
+    else:
+        cands += [("bwd (all kernels)", bwd_ms, f_bwd)]
+    name, kms, kfl = max(cands, key=lambda c: c[1])
+    dominant = (name, kfl / (kms * 1e-3) / 1e12, kms, kfl)
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as fh:
-            traffic = json.load(fh).get(f"{args.workload}_{dominant[0]}")
+            traffic = json.load(fh).get(f"{args.workload}_{name}")
     except Exception:
         pass
     if rank != 0:
@@ -336,7 +364,8 @@ def run_ours(args, w):
         "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf, "pct_of_peak": 100.0 * value / world / peak,
         "roofline": {"bound": "tensor", "kernel": dominant[0], "achieved": dominant[1], "peak": peak,
                      "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": dominant[1] / peak, "traffic": traffic,
-                     "ms_per_launch": dominant[2], "flops_per_launch": dominant[3]},
+                     "ms_per_launch": dominant[2], "flops_per_launch": dominant[3],
+                     "kernel_ms": kernel_ms, "traffic_source": "profiles/traffic_cfg4.md (ncu, scaled)"},
         "e2e": {"value": world * (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": launches[0],

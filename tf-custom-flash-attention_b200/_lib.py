@@ -54,6 +54,8 @@ def lib() -> ctypes.CDLL:
     L.sdpa_b200_path.restype = ci
     L.sdpa_b200_last_launch_count.restype = ci
     L.sdpa_b200_version.restype = ci
+    L.sdpa_b200_set_bwd_events.argtypes = [vp, ci]
+    L.sdpa_b200_set_bwd_events.restype = ci
     _lib = L
     return L
 
@@ -67,5 +69,5 @@ EXPORTS = (
     "sdpa_b200_fwd", "sdpa_b200_bwd_workspace_bytes", "sdpa_b200_bwd", "sdpa_b200_dropout_mask",
     "sdpa_b200_strerror", "sdpa_b200_device_status", "sdpa_b200_set_wait_timeout_ns",
     "sdpa_b200_test_wait_timeout", "sdpa_b200_path", "sdpa_b200_last_launch_count", "sdpa_b200_version",
-    "sdpa_b200_bwd_noalloc", "sdpa_b200_bwd_dstats",
+    "sdpa_b200_bwd_noalloc", "sdpa_b200_bwd_dstats", "sdpa_b200_set_bwd_events",
 )

@@ -16,11 +16,14 @@
 using namespace sdpa_b200;
 using namespace sdpa_b200::host;
 
+thread_local void* const* sdpa_b200::t_bwd_events = nullptr;
+
 namespace {
 
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
 std::atomic<uint64_t> g_timeout_ns{kDefaultTimeoutNs};
 thread_local int t_launches = 0;
+thread_local void* t_bwd_event_store[4];  // copy of the caller's events
 
 bool force_simt() {
   const char* e = std::getenv("SDPA_B200_FORCE_SIMT");
@@ -244,6 +247,17 @@ int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
 }
 
 int sdpa_b200_last_launch_count(void) { return t_launches; }
+
+int sdpa_b200_set_bwd_events(void* const* events, int n) {
+  if (!events) {
+    t_bwd_events = nullptr;
+    return SDPA_B200_OK;
+  }
+  if (n != 4) return SDPA_B200_EINVAL;
+  for (int i = 0; i < 4; ++i) t_bwd_event_store[i] = events[i];
+  t_bwd_events = t_bwd_event_store;
+  return SDPA_B200_OK;
+}
 
 int sdpa_b200_version(void) { return 100; }
 

@@ -74,6 +74,12 @@ inline int launch_result() {
 
 }  // namespace host
 
+// Optional events recorded between the backward's launches (diagnostic).
+extern thread_local void* const* t_bwd_events;
+inline void record_bwd_event(int i, cudaStream_t st) {
+  if (t_bwd_events) cudaEventRecord(static_cast<cudaEvent_t>(t_bwd_events[i]), st);
+}
+
 // Launchers, one per translation unit (launch count added to *launches).
 int launch_fwd_tc(const Params& p, cudaStream_t st, int* launches);
 int launch_bwd_tc(const Params& p, cudaStream_t st, int* launches);
