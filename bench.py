@@ -286,17 +286,12 @@ def run_ours(args, w):
     d2h = 0
 
     def e2e_step():
+        # public host-buffer API: batch chunks pipelined over copy-in / compute / copy-out streams
         nonlocal outs_h, d2h
-        dq_, dk_, dv_ = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
-        ddo = hdo.to(dev, non_blocking=True)
-        o, s = fa.sdpa(dq_, dk_, dv_, w["seed"], offset, **kw)
-        gq, gk, gv = fa.sdpa_grad(dq_, dk_, dv_, o, s, ddo, w["seed"], offset, **kw)
-        res = [o, s, gq, gk, gv]
-        if outs_h is None:
-            outs_h = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in res]
-            d2h = sum(x.numel() * x.element_size() for x in res)
-        for hbuf, x in zip(outs_h, res):
-            hbuf.copy_(x, non_blocking=True)
+        outs_h = fa.pipeline.train_step_host(hq, hk, hv, hdo, w["seed"], offset, scale=kw["scale"],
+                                             dropout=kw["dropout"], causal_mask=kw["causal_mask"], chunks=4,
+                                             device=dev, out=outs_h)
+        d2h = sum(x.numel() * x.element_size() for x in outs_h)
 
     e2e_steps = max(1, min(args.steps, 5))
     for _ in range(min(args.warmup, 2)):

@@ -61,3 +61,19 @@ def test_full_size_against_dense(B, S, D, causal, p, rows):
             assert rel(a, r) <= 2e-3, (name, b, rel(a, r))
         del keep, ref
     torch.cuda.synchronize()
+
+
+def test_host_pipeline_matches_device_calls():
+    """train_step_host (chunked, overlapped copies) equals one device call on the whole batch."""
+    B, S, D = 6, 512, 128
+    g = torch.Generator().manual_seed(9)
+    hq, hk, hv, hdo = (torch.randn(B, S, D, generator=g).half().pin_memory() for _ in range(4))
+    kw = dict(scale=D ** -0.5, dropout=0.1, causal_mask=True)
+    outs = fa.pipeline.train_step_host(hq, hk, hv, hdo, 5, 123, chunks=4, **kw)
+    torch.cuda.synchronize()
+    q, k, v, do = (x.cuda() for x in (hq, hk, hv, hdo))
+    o, s = fa.sdpa(q, k, v, 5, 123, **kw)
+    g2 = fa.sdpa_grad(q, k, v, o, s, do, 5, 123, dropout=0.1, scale=D ** -0.5, causal_mask=True)
+    torch.cuda.synchronize()
+    for a, b in zip(outs, (o, s) + tuple(g2)):
+        assert torch.equal(a, b.cpu())

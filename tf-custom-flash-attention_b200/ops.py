@@ -68,8 +68,10 @@ _FEATURE_MSG = ("CUDA kernel does not support feature size over 128. Set smaller
 
 
 def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seed, offset, scale: float = 1.0, dropout: float = 0.0,
-         causal_mask: bool = False):
-    """The ``Sdpa`` op: returns (output [B,S_q,D_v] T, stats [B,S_q] float32)."""
+         causal_mask: bool = False, *, _out=None):
+    """The ``Sdpa`` op: returns (output [B,S_q,D_v] T, stats [B,S_q] float32).
+
+    ``_out`` (internal): preallocated (output, stats) to write into."""
     for i, t in enumerate((q, k, v)):
         _rank3(t, i)
     seed_v = _scalar_u64(seed, "seed")
@@ -89,8 +91,11 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seed, offset, scale:
     if max(D_qk, D_v) > 128:
         raise InvalidArgumentError(_FEATURE_MSG)
     (q, k, v), dt = _prep([q, k, v])
-    out = torch.empty((B, S_q, D_v), dtype=q.dtype, device=q.device)
-    stats = torch.empty((B, S_q), dtype=torch.float32, device=q.device)
+    if _out is not None:
+        out, stats = _out
+    else:
+        out = torch.empty((B, S_q, D_v), dtype=q.dtype, device=q.device)
+        stats = torch.empty((B, S_q), dtype=torch.float32, device=q.device)
     if B * S_q == 0 or D_v == 0:
         return out, stats
     with torch.cuda.device(q.device):
@@ -103,11 +108,12 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seed, offset, scale:
 
 
 def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale: float = 1.0,
-              causal_mask: bool = False, *, d_stats=None):
+              causal_mask: bool = False, *, d_stats=None, _out=None, _ws=None):
     """The ``SdpaGrad`` op: returns (dq, dk, dv) shaped like (q, k, v).
 
     ``d_stats`` (extension, not in the reference): a float32 [B, S_q] gradient
-    reaching ``stats``; it is propagated as the log-sum-exp it is."""
+    reaching ``stats``; it is propagated as the log-sum-exp it is.
+    ``_out`` / ``_ws`` (internal): preallocated (dq, dk, dv) and float32 workspace."""
     for i, t in enumerate((q, k, v)):
         _rank3(t, i)
     seed_v = _scalar_u64(seed, "seed")
@@ -137,10 +143,13 @@ def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale
     if stats.dtype != torch.float32 or not stats.is_cuda:
         raise InvalidArgumentError("stats must be a float32 CUDA tensor")
     stats = stats.contiguous()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dq, dk, dv = _out if _out is not None else (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v))
     L = _lib.lib()
     ws_bytes = L.sdpa_b200_bwd_workspace_bytes(dt, B, S_q, S_kv, D_qk, D_v)
-    ws = torch.empty((max(ws_bytes, 4) + 3) // 4, dtype=torch.float32, device=q.device)
+    if _ws is not None and _ws.numel() * 4 >= ws_bytes:
+        ws = _ws
+    else:
+        ws = torch.empty((max(ws_bytes, 4) + 3) // 4, dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
         st = torch.cuda.current_stream().cuda_stream
         if d_stats is None:
