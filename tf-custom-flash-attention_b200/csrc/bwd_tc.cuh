@@ -14,9 +14,10 @@
 //   dP = dO V^T, dS as above, dQ += dS K (TS MMA); dQ *= scale at the end
 //   (layout and pipeline at its definition below).
 //
-// Roles (320 threads): warps 0-7 elementwise (warp w serves TMEM lanes
-// 32*(w%4).. and column half w/4 of each 64-column tile), warp 8 TMA
-// producer, warp 9 MMA issuer + TMEM owner.  S / dP are double-buffered in
+// Roles: warps 0-7 elementwise (warp w serves TMEM lanes 32*(w%4).. and
+// column half w/4 of each 64-column tile), warp 8 TMA producer, warp 9 MMA
+// issuer + TMEM owner; dkdv_kernel adds warp 10, which issues the gradient
+// MMAs while warp 9 issues the score MMAs.  S / dP are double-buffered in
 // TMEM so the MMAs of tile j+1 overlap the elementwise work of tile j.
 //
 // Semantics: sdpa/sdpa_bwd.cu.cc:125-170 (dS formulas, skip rule, dropout).
@@ -29,6 +30,7 @@ namespace sdpa_b200 {
 namespace tc {
 
 constexpr int kBwdThreads = 320;
+constexpr int kDkdvThreads = 352;  // + a second MMA-issuing warp
 constexpr int kBwdRows = 128;   // rows owned by a CTA (TMEM lanes)
 constexpr int kBwdTile = 64;    // rows of each streamed tile
 constexpr int kBwdStages = 3;
@@ -66,6 +68,8 @@ struct BwdBarriers {
   uint64_t vec_ready[2];
   uint64_t acc_done;
   uint64_t mma_done;
+  uint64_t g_done[2];    // dK/dV kernel: gradient MMAs of the tile in S/dP buffer sb completed
+  uint64_t mma_done2;    // dK/dV kernel: drain of the second issuing thread
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -85,6 +89,9 @@ __device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols,
     }
     mbar_init(&bars->acc_done, 1);
     mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->g_done[0], 1);
+    mbar_init(&bars->g_done[1], 1);
+    mbar_init(&bars->mma_done2, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -255,7 +262,7 @@ __device__ __forceinline__ void dq_elems(const uint32_t* sv, const uint32_t* dpv
 }
 
 template <int DQK, int DV, bool DROP>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kDkdvThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do, const Params p) {
   using Cfg = BwdCfg<DQK, DV>;
@@ -282,11 +289,39 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_k, &tm_v, &tm_q, &tm_do, static_cast<int>(n0), tile0, nq,
                                  static_cast<int>(b), ctl, p.timeout_ns);
   } else if (warp == 9) {
+    // Score MMAs.  S^T / dP^T of tile t go to buffer t&1, which the gradient
+    // MMAs of tile t-2 read (as P~^T / dS^T): wait until those completed.
     if (lane == 0 && nq > 0) {
       bool ok = mbar_wait(&bars->res_full, 0, ctl);
-      auto grads = [&](int t) -> bool {
+      for (int t = 0; ok && t < nq; ++t) {
         const int s = t % kBwdStages, sb = t & 1;
-        if (!mbar_wait(&bars->p_full[sb], (t >> 1) & 1, ctl)) return false;
+        if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl) ||
+            (t >= 2 && !mbar_wait(&bars->g_done[sb], ((t >> 1) - 1) & 1, ctl))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S^T = K Q^T, dP^T = V dO^T
+        mma_commit(&bars->s_full[sb]);
+      }
+      mma_commit(&bars->mma_done);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else if (warp == 10) {
+    // Gradient MMAs, issued from their own thread so that its waits overlap
+    // the score MMAs in the tensor pipe (and the other way round).
+    if (lane == 0 && nq > 0) {
+      bool ok = true;
+      for (int t = 0; ok && t < nq; ++t) {
+        const int s = t % kBwdStages, sb = t & 1;
+        if (!mbar_wait(&bars->p_full[sb], (t >> 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         // dV += P~^T dO_t ; dK += dS^T Q_t
         bwd_issue_acc<DV>(tmem + Cfg::kAcc0, tmem + Cfg::kS + sb * kBwdTile, sbase + Cfg::kStBOff + s * Cfg::kStB,
@@ -294,27 +329,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bwd_issue_acc<DQK>(tmem + Cfg::kAcc1, tmem + Cfg::kDP + sb * kBwdTile, sbase + Cfg::kStAOff + s * Cfg::kStA,
                            t == 0);
         mma_commit(&bars->st_empty[s]);
-        return true;
-      };
-      for (int t = 0; ok && t < nq; ++t) {
-        const int s = t % kBwdStages, sb = t & 1;
-        if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S^T = K Q^T, dP^T = V dO^T
-        mma_commit(&bars->s_full[sb]);
-        if (t > 0 && !grads(t - 1)) ok = false;
+        mma_commit(&bars->g_done[sb]);
       }
-      if (ok) ok = grads(nq - 1);
       mma_commit(&bars->acc_done);
-      mma_commit(&bars->mma_done);
+      mma_commit(&bars->mma_done2);
       WaitCtl drain = ctl;
       drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
       int dummy = 0;
       drain.abort_flag = &dummy;
-      mbar_wait(&bars->mma_done, 0, drain);
+      mbar_wait(&bars->mma_done2, 0, drain);
     }
   } else {
     // ------------------------------------------------ elementwise warps
