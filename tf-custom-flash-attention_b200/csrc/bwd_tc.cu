@@ -36,11 +36,11 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   const int64_t gq = ((p.S_q + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
   if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
   sdpa_b200::record_bwd_event(1, st);
-  kkv<<<static_cast<unsigned>(gkv), tc::kDkdvThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
+  kkv<<<static_cast<unsigned>(gkv), tc::kBwdTcThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
   ++*launches;
   if (int r = launch_result()) return r;
   sdpa_b200::record_bwd_event(2, st);
-  kq<<<static_cast<unsigned>(gq), tc::kBwdThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
+  kq<<<static_cast<unsigned>(gq), tc::kBwdTcThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
   ++*launches;
   sdpa_b200::record_bwd_event(3, st);
   return launch_result();

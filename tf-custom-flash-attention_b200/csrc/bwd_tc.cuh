@@ -30,7 +30,7 @@ namespace sdpa_b200 {
 namespace tc {
 
 constexpr int kBwdThreads = 320;
-constexpr int kDkdvThreads = 352;  // + a second MMA-issuing warp
+constexpr int kBwdTcThreads = 352;  // dK/dV and dQ kernels: + a second MMA-issuing warp
 constexpr int kBwdRows = 128;   // rows owned by a CTA (TMEM lanes)
 constexpr int kBwdTile = 64;    // rows of each streamed tile
 constexpr int kBwdStages = 3;
@@ -262,7 +262,7 @@ __device__ __forceinline__ void dq_elems(const uint32_t* sv, const uint32_t* dpv
 }
 
 template <int DQK, int DV, bool DROP>
-__global__ void __launch_bounds__(kDkdvThreads, 1)
+__global__ void __launch_bounds__(kBwdTcThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do, const Params p) {
   using Cfg = BwdCfg<DQK, DV>;
@@ -426,13 +426,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 }
 
 // ============================================================================
-// dQ kernel with 128-key tiles.  One CTA = 128 query rows; per key tile t:
+// dQ kernel with 128-key tiles.  One CTA = 128 query rows; per key tile t
+// (warp 9 issues S/dP, warp 10 issues dQ):
 //     S = Q K_t^T, dP = dO V_t^T      (SS MMA, N = 128: full rate)
 //     dS = p (kf dP - D)               (8 elementwise warps, 64 columns each)
 //     dQ += dS K_t                     (TS MMA, A = dS from its own TMEM buffer)
 // The elementwise warps release S/dP as soon as they have loaded them, so the
 // MMAs of tile t+1 run while dS of tile t is computed.  TMEM: dQ [0,128),
-// dS [128,192) (fp16 pairs), S [256,384), dP [384,512).  K is held until dQ
+// dS [128,256) (two buffers of fp16 pairs), S [256,384), dP [384,512).  K is held until dQ
 // consumed it (3-stage ring), V only until dP (2 stages); Q and dO resident.
 template <int DQK, int DV>
 struct Dq2Cfg {
@@ -454,14 +455,14 @@ struct Dq2Barriers {
   uint64_t res_full;
   uint64_t k_full[3], k_empty[3];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full, sdp_free, ds_full, ds_empty;
-  uint64_t acc_done, mma_done;
+  uint64_t s_full, sdp_free, ds_full[2], ds_empty[2];
+  uint64_t acc_done, mma_done, mma_done2;
   uint32_t tmem_base;
   int abort_flag;
 };
 
 template <int DQK, int DV, bool DROP>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kBwdTcThreads, 1)
     dq2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using Cfg = Dq2Cfg<DQK, DV>;
@@ -489,10 +490,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->sdp_free, 256);
-    mbar_init(&bars->ds_full, 256);
-    mbar_init(&bars->ds_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->ds_full[s], 256);
+      mbar_init(&bars->ds_empty[s], 1);
+    }
     mbar_init(&bars->acc_done, 1);
     mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->mma_done2, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -548,14 +552,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------- MMA issuer
+    // ------------------------------------------- score MMA issuer (S, dP)
     if (lane == 0 && nkv > 0) {
       constexpr uint32_t idesc_s = make_idesc(kBwdRows, TN, false, false, false);
-      constexpr uint32_t idesc_dq = make_idesc(kBwdRows, DQK, false, true, false);
-      auto issue_scores = [&](int t) -> bool {
+      bool ok = mbar_wait(&bars->res_full, 0, ctl);
+      for (int t = 0; ok && t < nkv; ++t) {
         const int ks = t % 3, vs = t & 1;
-        if (!mbar_wait(&bars->k_full[ks], (t / 3) & 1, ctl)) return false;
-        if (!mbar_wait(&bars->v_full[vs], (t >> 1) & 1, ctl)) return false;
+        // S/dP of tile t-1 must be in registers of the elementwise warps
+        if ((t > 0 && !mbar_wait(&bars->sdp_free, (t - 1) & 1, ctl)) || !mbar_wait(&bars->k_full[ks], (t / 3) & 1, ctl) ||
+            !mbar_wait(&bars->v_full[vs], (t >> 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t kb = sbase + Cfg::kKOff + ks * Cfg::kKBytes, vb = sbase + Cfg::kVOff + vs * Cfg::kVBytes;
         const uint32_t qb = sbase + Cfg::kQOff, ob = sbase + Cfg::kOOff;
@@ -573,30 +581,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         mma_commit(&bars->v_empty[vs]);  // V_t is no longer read
         mma_commit(&bars->s_full);
-        return true;
-      };
-      bool ok = mbar_wait(&bars->res_full, 0, ctl) && issue_scores(0);
-      for (int t = 0; ok && t < nkv; ++t) {
-        // S/dP of tile t are in registers of the elementwise warps: start tile t+1
-        if (!mbar_wait(&bars->sdp_free, t & 1, ctl)) { ok = false; break; }
-        if (t + 1 < nkv && !issue_scores(t + 1)) { ok = false; break; }
-        if (!mbar_wait(&bars->ds_full, t & 1, ctl)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t kb = sbase + Cfg::kKOff + (t % 3) * Cfg::kKBytes;
-#pragma unroll
-        for (int kk = 0; kk < TN / 16; ++kk)
-          mma_f16_ts(tmem + Cfg::kDQ, tmem + Cfg::kDS + kk * 8, make_sw128_desc(kb + kk * 16 * 128, TN * 128, 1024),
-                     idesc_dq, (t > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars->k_empty[t % 3]);
-        mma_commit(&bars->ds_empty);
       }
-      mma_commit(&bars->acc_done);
       mma_commit(&bars->mma_done);
       WaitCtl drain = ctl;
       drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
       int dummy = 0;
       drain.abort_flag = &dummy;
       mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else if (warp == 10) {
+    // -------------------------------------------- dQ MMA issuer (dQ += dS K)
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t idesc_dq = make_idesc(kBwdRows, DQK, false, true, false);
+      bool ok = true;
+      for (int t = 0; ok && t < nkv; ++t) {
+        const int db = t & 1;
+        if (!mbar_wait(&bars->ds_full[db], (t >> 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = sbase + Cfg::kKOff + (t % 3) * Cfg::kKBytes;
+#pragma unroll
+        for (int kk = 0; kk < TN / 16; ++kk)
+          mma_f16_ts(tmem + Cfg::kDQ, tmem + Cfg::kDS + db * 64 + kk * 8,
+                     make_sw128_desc(kb + kk * 16 * 128, TN * 128, 1024), idesc_dq, (t > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars->k_empty[t % 3]);
+        mma_commit(&bars->ds_empty[db]);
+      }
+      mma_commit(&bars->acc_done);
+      mma_commit(&bars->mma_done2);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + p.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done2, 0, drain);
     }
   } else {
     // ------------------------------------------------ elementwise warps
@@ -641,18 +660,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         else
           dq_elems<DROP, false>(sv + 32 * h2, dpv + 32 * h2, lim, sl2, lse2, delta, dp_inv, st, thr_m1, dk + 16 * h2);
       }
-      if (t > 0) {  // dQ of the previous tile must have read the dS buffer
-        if (!warp_wait(&bars->ds_empty, (t - 1) & 1, ctl)) {
+      const int db = t & 1;
+      if (t > 1) {  // dQ of tile t-2 must have read dS buffer db
+        if (!warp_wait(&bars->ds_empty[db], ((t >> 1) - 1) & 1, ctl)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + half * 32, dk);
-      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + half * 32 + 16, (dk + 16));
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + db * 64 + half * 32, dk);
+      SDPA_TMEM_ST16(tmem + lane_base + Cfg::kDS + db * 64 + half * 32 + 16, (dk + 16));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->ds_full);
+      mbar_arrive(&bars->ds_full[db]);
     }
     if (ok && nkv > 0) ok = warp_wait(&bars->acc_done, 0, ctl);
     if (ok) {
