@@ -610,9 +610,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (c >= lim) r[c] = __float_as_uint(-INFINITY);
       }
-      float tmax_raw = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
-      for (int c = 0; c < 128; ++c) tmax_raw = fmaxf(tmax_raw, __uint_as_float(r[c]));
+      for (int c = 0; c < 128; c += 8)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], __uint_as_float(r[c + 2 * q]), __uint_as_float(r[c + 2 * q + 1]));
+      const float tmax_raw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float tmax = tmax_raw * sl;
       m_run = fmaxf(m_run, tmax);
       float alpha = 1.0f;
@@ -624,31 +627,36 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         l *= alpha;
       }
       const float mu = (m_use == -INFINITY) ? 0.0f : m_use;
-      float rs = 0.0f;
-      // P packed in place: r[c/2] <- (p_c, p_c+1) once both are read
+      // P packed in place: r[c/2] <- (p_c, p_c+1) once both are read.  With
+      // dropout (issue-bound) argument and row sum go in packed pairs; four
+      // partial sums keep the add chains short.
+      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const float nmu = -mu;
       if (DROP) {
         LcgWalk st(lcg_state(rbase, static_cast<uint64_t>(kv0)));
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
-          const float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
-          rs += p0 + p1;
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(r[c]), __uint_as_float(r[c + 1]), sl, sl, nmu, nmu);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          const int q = (c >> 1) & 1;
+          fadd2(rs[2 * q], rs[2 * q + 1], p0, p1);
           const bool d0 = st.dropped(thr_m1);
           st.step();
           const bool d1 = st.dropped(thr_m1);
           st.step();
           r[c / 2] = pack_half2(d0 ? 0.0f : p0, d1 ? 0.0f : p1);
         }
-      } else {
+      } else {  // bound by MUFU and the tensor pipe, not by issue: scalar forms
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, -mu));
-          const float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, -mu));
-          rs += p0 + p1;
+          const float p0 = ex2(fmaf(__uint_as_float(r[c]), sl, nmu));
+          const float p1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl, nmu));
+          rs[(c >> 1) & 3] += p0 + p1;
           r[c / 2] = pack_half2(p0, p1);
         }
       }
-      l += rs;
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       SDPA_TMEM_ST32(tS + 0, (r + 0));
       SDPA_TMEM_ST32(tS + 32, (r + 32));
       if (__any_sync(0xffffffffu, rescale_o)) {

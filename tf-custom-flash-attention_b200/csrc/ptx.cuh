@@ -227,6 +227,30 @@ __device__ __forceinline__ bool dropped(uint64_t state, uint64_t thr) { return (
 
 // The same walk on the two 32-bit halves of the state: one step adds A with a
 // carry from the low word (2 instructions); the drop test reads the high word.
+// Packed fp32 pairs (sm_100 f32x2 ALU forms): one instruction for two lanes
+// of work.  Same rounding as the scalar forms (round-to-nearest).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1) {  // (d0, d1) += (a0, a1)
+  asm("{\n\t.reg .b64 a, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 d, {%0, %1};\n\t"
+      "add.rn.f32x2 d, d, a;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
+// Three-input maximum (exact).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 struct LcgWalk {
   uint32_t lo, hi;
   __device__ __forceinline__ explicit LcgWalk(uint64_t s)
