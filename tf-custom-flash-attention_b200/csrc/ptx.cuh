@@ -244,6 +244,13 @@ __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1) 
       : "+f"(d0), "+f"(d1)
       : "f"(a0), "f"(a1));
 }
+__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 // Three-input maximum (exact).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
