@@ -76,6 +76,27 @@ int sdpa_b200_bwd_dstats(int dtype, const void* q, const void* k, const void* v,
                          int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal, uint64_t seed,
                          uint64_t offset, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Head-strided layout for the multi-head layer: q [B,S_q,H,D_qk], k
+ * [B,S_kv,H,D_qk], v [B,S_kv,H,D_v], out / d_out [B,S_q,H,D_v] and dq, dk, dv
+ * shaped like q, k, v, read and written in place (no transposes); stats,
+ * d_stats and the workspace are [B,H,S_q] (workspace bytes as for B*H rows).
+ * Results equal sdpa_b200_fwd / _bwd_dstats on the [B*H,S,D] tensors that the
+ * reference's MHA builds by transposing (sdpa/mha.py:103-129, heads innermost
+ * in the folded batch index, which is also the dropout counter's).  No
+ * counterpart in the reference, whose op takes only [B,S,D]. */
+int sdpa_b200_fwd_bshd(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
+                       int64_t H, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
+                       int causal, uint64_t seed, uint64_t offset, void* stream);
+int sdpa_b200_bwd_bshd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                       const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                       int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
+                       uint64_t seed, uint64_t offset, void* workspace, size_t workspace_bytes, void* stream);
+
+/* What the last SDPA_B200_ECUDA returned on the calling thread came from (the
+ * CUDA error name, or the TMA descriptor encode result); "" before any.
+ * Diagnostic, no reference counterpart. */
+const char* sdpa_b200_last_error_detail(void);
+
 /* Writes mask[b][i][j] = 1 where (b,i,j) is dropped, from the same device RNG
  * routine the kernels use (diagnostic; no reference counterpart beyond the
  * RNG of sdpa/sdpa_utils.cuh:13-19).  mask is a device uint8 [B,S_q,S_kv]. */

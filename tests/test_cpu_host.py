@@ -76,3 +76,13 @@ def test_host_validation_messages():
         fa.sdpa(torch.zeros(4, 8), x, x, 0, 0)
     with pytest.raises(fa.InvalidArgumentError, match="CUDA tensors only"):
         fa.sdpa(x, x, x, 0, 0)  # no CPU kernel: fails loudly
+
+
+def test_bshd_validation_on_host():
+    """sdpa_bshd checks ranks and head counts before touching a device."""
+    torch = pytest.importorskip("torch")
+    q = torch.zeros(2, 8, 4, 16)
+    with pytest.raises(fa.InvalidArgumentError, match="rank 4"):
+        fa.sdpa_bshd(q[0], q, q, 0, 0)
+    with pytest.raises(fa.InvalidArgumentError, match="head count"):
+        fa.sdpa_bshd(q, torch.zeros(2, 8, 3, 16), q, 0, 0)

@@ -8,10 +8,10 @@ Kernels live in csrc/ and are reached through the C ABI of include/sdpa_b200.h
 (libsdpa_b200.so, built in-tree by build.py).
 """
 from .ops import (InvalidArgumentError, KernelError, device_status, dropout_mask, kernel_path, last_launch_count,
-                  sdpa, sdpa_grad)
+                  sdpa, sdpa_bshd, sdpa_grad, sdpa_grad_bshd)
 from . import autograd, pipeline, sharding  # noqa: F401
 from .mha import MHA  # noqa: F401
 from ._lib import LIB_PATH  # noqa: F401
 
-__all__ = ["sdpa", "sdpa_grad", "dropout_mask", "device_status", "kernel_path", "last_launch_count",
+__all__ = ["sdpa", "sdpa_grad", "sdpa_bshd", "sdpa_grad_bshd", "dropout_mask", "device_status", "kernel_path", "last_launch_count",
            "InvalidArgumentError", "KernelError", "autograd", "pipeline", "sharding", "MHA"]

@@ -40,6 +40,14 @@ def lib() -> ctypes.CDLL:
     L.sdpa_b200_bwd_noalloc.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, f32,
                                         ci, u64, u64, vp]
     L.sdpa_b200_bwd_noalloc.restype = ci
+    L.sdpa_b200_fwd_bshd.argtypes = [ci, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, f32, f32, ci, u64, u64,
+                                     vp]
+    L.sdpa_b200_fwd_bshd.restype = ci
+    L.sdpa_b200_bwd_bshd.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, f32,
+                                     f32, ci, u64, u64, vp, sz, vp]
+    L.sdpa_b200_bwd_bshd.restype = ci
+    L.sdpa_b200_last_error_detail.argtypes = []
+    L.sdpa_b200_last_error_detail.restype = ctypes.c_char_p
     L.sdpa_b200_dropout_mask.argtypes = [u64, u64, i64, i64, i64, f32, vp, vp]
     L.sdpa_b200_dropout_mask.restype = ci
     L.sdpa_b200_strerror.argtypes = [ci]
@@ -69,5 +77,6 @@ EXPORTS = (
     "sdpa_b200_fwd", "sdpa_b200_bwd_workspace_bytes", "sdpa_b200_bwd", "sdpa_b200_dropout_mask",
     "sdpa_b200_strerror", "sdpa_b200_device_status", "sdpa_b200_set_wait_timeout_ns",
     "sdpa_b200_test_wait_timeout", "sdpa_b200_path", "sdpa_b200_last_launch_count", "sdpa_b200_version",
-    "sdpa_b200_bwd_noalloc", "sdpa_b200_bwd_dstats", "sdpa_b200_set_bwd_events",
+    "sdpa_b200_bwd_noalloc", "sdpa_b200_bwd_dstats", "sdpa_b200_set_bwd_events", "sdpa_b200_fwd_bshd",
+    "sdpa_b200_bwd_bshd", "sdpa_b200_last_error_detail",
 )

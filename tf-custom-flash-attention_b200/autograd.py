@@ -36,6 +36,31 @@ class SdpaFunction(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None, None
 
 
+class SdpaBSHDFunction(torch.autograd.Function):
+    """Same gradient registration over head-strided [B,S,H,D] tensors (ops.sdpa_bshd)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, seed, offset, dropout, scale, causal_mask):
+        o, s = ops.sdpa_bshd(q, k, v, seed, offset, scale=scale, dropout=dropout, causal_mask=causal_mask)
+        ctx.save_for_backward(q, k, v, o, s)
+        ctx.attrs = (int(ops._scalar_u64(seed, "seed")), int(ops._scalar_u64(offset, "offset")), dropout, scale,
+                     causal_mask)
+        return o
+
+    @staticmethod
+    def backward(ctx, d_o):
+        q, k, v, o, s = ctx.saved_tensors
+        seed, offset, dropout, scale, causal = ctx.attrs
+        dq, dk, dv = ops.sdpa_grad_bshd(q, k, v, o, s, d_o.contiguous(), seed, offset, dropout=dropout, scale=scale,
+                                        causal_mask=causal)
+        return dq, dk, dv, None, None, None, None, None
+
+
+def sdpa_bshd(q, k, v, seed, offset, dropout: float = 0.0, scale: float = 1.0, causal_mask: bool = False):
+    """Differentiable attention over [B,S,H,D] tensors (no head transposes); returns [B,S_q,H,D_v]."""
+    return SdpaBSHDFunction.apply(q, k, v, seed, offset, dropout, scale, causal_mask)
+
+
 def sdpa(q, k, v, seed, offset, dropout: float = 0.0, scale: float = 1.0, causal_mask: bool = False):
     """Differentiable attention, like mha.py:24-29 ``sdpa`` (returns the output only)."""
     o, _ = SdpaFunction.apply(q, k, v, seed, offset, dropout, scale, causal_mask)

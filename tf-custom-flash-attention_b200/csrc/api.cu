@@ -25,6 +25,17 @@ std::atomic<uint64_t> g_timeout_ns{kDefaultTimeoutNs};
 thread_local int t_launches = 0;
 thread_local void* t_bwd_event_store[4];  // copy of the caller's events
 
+// The TMA descriptors are encoded through the driver API, which needs a
+// current context on the calling thread.  A thread that has made no runtime
+// call yet (e.g. an autograd worker whose device guard saw the device already
+// selected) has none: cudaSetDevice binds the device's primary context.
+int bind_context() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaSetDevice(dev);
+  return e == cudaSuccess ? SDPA_B200_OK : cuda_failure("binding the device context", e);
+}
+
 bool force_simt() {
   const char* e = std::getenv("SDPA_B200_FORCE_SIMT");
   return e && e[0] == '1';
@@ -50,6 +61,7 @@ Params make_params(int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D
   Params p;
   std::memset(&p, 0, sizeof(p));
   p.B = B;
+  p.H = 1;
   p.S_q = S_q;
   p.S_kv = S_kv;
   p.D_qk = static_cast<int>(D_qk);
@@ -124,22 +136,43 @@ __global__ void wait_timeout_kernel(uint64_t timeout_ns) {
 
 extern "C" {
 
-int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
-                  int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
-                  uint64_t seed, uint64_t offset, void* stream) {
+static int fwd_impl(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
+                    int64_t H, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
+                    int causal, uint64_t seed, uint64_t offset, void* stream) {
   t_launches = 0;
   if (int r = check_common(dtype, B, S_q, S_kv, D_qk, D_v, causal)) return r;
+  if (H < 1 || B % H != 0) return SDPA_B200_EINVAL;
   if (B == 0 || S_q == 0) return SDPA_B200_OK;
   if (!out || !stats || (S_kv > 0 && (!q || !k || !v))) return SDPA_B200_EINVAL;
   Params p = make_params(B, S_q, S_kv, D_qk, D_v, scale, dropout, causal, seed, offset);
+  p.H = H;
   p.q = q;
   p.k = k;
   p.v = v;
   p.out = out;
   p.stats = stats;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int r = bind_context()) return r;
   if (tc_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return launch_fwd_tc(p, st, &t_launches);
   return dtype == SDPA_B200_F16 ? launch_fwd_simt_f16(p, st, &t_launches) : launch_fwd_simt_f32(p, st, &t_launches);
+}
+
+int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
+                  int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
+                  uint64_t seed, uint64_t offset, void* stream) {
+  return fwd_impl(dtype, q, k, v, out, stats, B, 1, S_q, S_kv, D_qk, D_v, scale, dropout, causal, seed, offset,
+                  stream);
+}
+
+static bool bshd_batch(int64_t B, int64_t H) { return B >= 0 && H >= 1 && B <= 0x7fffffffLL / H; }
+
+int sdpa_b200_fwd_bshd(int dtype, const void* q, const void* k, const void* v, void* out, float* stats, int64_t B,
+                       int64_t H, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
+                       int causal, uint64_t seed, uint64_t offset, void* stream) {
+  t_launches = 0;
+  if (!bshd_batch(B, H)) return SDPA_B200_EINVAL;
+  return fwd_impl(dtype, q, k, v, out, stats, B * H, H, S_q, S_kv, D_qk, D_v, scale, dropout, causal, seed, offset,
+                  stream);
 }
 
 size_t sdpa_b200_bwd_workspace_bytes(int, int64_t B, int64_t S_q, int64_t, int64_t, int64_t) {
@@ -148,11 +181,12 @@ size_t sdpa_b200_bwd_workspace_bytes(int, int64_t B, int64_t S_q, int64_t, int64
 }
 
 static int bwd_impl(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
-                    const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
-                  int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
-                  void* workspace, size_t workspace_bytes, void* stream) {
+                    const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                    int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
+                    uint64_t seed, uint64_t offset, void* workspace, size_t workspace_bytes, void* stream) {
   t_launches = 0;
   if (int r = check_common(dtype, B, S_q, S_kv, D_qk, D_v, causal)) return r;
+  if (H < 1 || B % H != 0) return SDPA_B200_EINVAL;
   if (B == 0 || (S_q == 0 && S_kv == 0)) return SDPA_B200_OK;
   const size_t need = sdpa_b200_bwd_workspace_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
   if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u)))
@@ -160,6 +194,7 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if ((S_q > 0 && (!q || !out || !stats || !d_out || !dq)) || (S_kv > 0 && (!k || !v || !dk || !dv)))
     return SDPA_B200_EINVAL;
   Params p = make_params(B, S_q, S_kv, D_qk, D_v, scale, dropout, causal, seed, offset);
+  p.H = H;
   p.q = q;
   p.k = k;
   p.v = v;
@@ -172,6 +207,7 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   p.delta = static_cast<float*>(workspace);
   p.d_stats = d_stats;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int r = bind_context()) return r;
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
   return dtype == SDPA_B200_F16 ? launch_bwd_simt_f16(p, st, &t_launches) : launch_bwd_simt_f32(p, st, &t_launches);
@@ -181,17 +217,29 @@ int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const 
                   const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
                   int64_t D_v, float scale, float dropout, int causal, uint64_t seed, uint64_t offset,
                   void* workspace, size_t workspace_bytes, void* stream) {
-  return bwd_impl(dtype, q, k, v, out, stats, nullptr, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,
-                  causal, seed, offset, workspace, workspace_bytes, stream);
+  return bwd_impl(dtype, q, k, v, out, stats, nullptr, d_out, dq, dk, dv, B, 1, S_q, S_kv, D_qk, D_v, scale,
+                  dropout, causal, seed, offset, workspace, workspace_bytes, stream);
 }
 
 int sdpa_b200_bwd_dstats(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
                          const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q,
                          int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal, uint64_t seed,
                          uint64_t offset, void* workspace, size_t workspace_bytes, void* stream) {
-  return bwd_impl(dtype, q, k, v, out, stats, d_stats, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,
-                  causal, seed, offset, workspace, workspace_bytes, stream);
+  return bwd_impl(dtype, q, k, v, out, stats, d_stats, d_out, dq, dk, dv, B, 1, S_q, S_kv, D_qk, D_v, scale,
+                  dropout, causal, seed, offset, workspace, workspace_bytes, stream);
 }
+
+int sdpa_b200_bwd_bshd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
+                       const float* d_stats, const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                       int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
+                       uint64_t seed, uint64_t offset, void* workspace, size_t workspace_bytes, void* stream) {
+  t_launches = 0;
+  if (!bshd_batch(B, H)) return SDPA_B200_EINVAL;
+  return bwd_impl(dtype, q, k, v, out, stats, d_stats, d_out, dq, dk, dv, B * H, H, S_q, S_kv, D_qk, D_v, scale,
+                  dropout, causal, seed, offset, workspace, workspace_bytes, stream);
+}
+
+const char* sdpa_b200_last_error_detail(void) { return t_err_detail; }
 
 int sdpa_b200_dropout_mask(uint64_t seed, uint64_t offset, int64_t B, int64_t S_q, int64_t S_kv, float dropout,
                            uint8_t* mask, void* stream) {

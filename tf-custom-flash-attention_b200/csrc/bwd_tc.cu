@@ -10,23 +10,23 @@ using namespace sdpa_b200::host;
 namespace {
 
 // tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
   using Cfg = tc::BwdCfg<DQK, DV>;
-  auto kkv = tc::dkdv_kernel<DQK, DV, DROP>;
-  auto kq = tc::dq2_kernel<DQK, DV, DROP>;
+  auto kkv = tc::dkdv_kernel<DQK, DV, DROP, HEADS>;
+  auto kq = tc::dq2_kernel<DQK, DV, DROP, HEADS>;
   using QCfg = tc::Dq2Cfg<DQK, DV>;
-  if (ensure_smem(kkv, Cfg::kSmemBytes, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (ensure_smem(kq, QCfg::kSmemBytes, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
+  if (cudaError_t e = ensure_smem(kkv, Cfg::kSmemBytes, attr_kv)) return cuda_failure("shared-memory attribute", e);
+  if (cudaError_t e = ensure_smem(kq, QCfg::kSmemBytes, attr_q)) return cuda_failure("shared-memory attribute", e);
   CUtensorMap k128, v128, q64, do64, q128, do128;
-  if (!make_map_f16(&k128, p.k, p.B, p.S_kv, p.D_qk, tc::kBwdRows) ||
-      !make_map_f16(&v128, p.v, p.B, p.S_kv, p.D_v, tc::kBwdRows) ||
-      !make_map_f16(&q64, p.q, p.B, p.S_q, p.D_qk, tc::kBwdTile) ||
-      !make_map_f16(&do64, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdTile) ||
-      !make_map_f16(&q128, p.q, p.B, p.S_q, p.D_qk, tc::kBwdRows) ||
-      !make_map_f16(&do128, p.d_o, p.B, p.S_q, p.D_v, tc::kBwdRows))
-    return SDPA_B200_ECUDA;
+  if (!make_map_f16(&k128, p.k, p.B, p.H, p.S_kv, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&v128, p.v, p.B, p.H, p.S_kv, p.D_v, tc::kBwdRows) ||
+      !make_map_f16(&q64, p.q, p.B, p.H, p.S_q, p.D_qk, tc::kBwdTile) ||
+      !make_map_f16(&do64, p.d_o, p.B, p.H, p.S_q, p.D_v, tc::kBwdTile) ||
+      !make_map_f16(&q128, p.q, p.B, p.H, p.S_q, p.D_qk, tc::kBwdRows) ||
+      !make_map_f16(&do128, p.d_o, p.B, p.H, p.S_q, p.D_v, tc::kBwdRows))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
   const int64_t rows = p.B * p.S_q;
   sdpa_b200::record_bwd_event(0, st);
   simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
@@ -46,9 +46,14 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   return launch_result();
 }
 
+// HEADS: [B/H, S, H, D] tensors (4-D TMA maps); else contiguous [B, S, D].
 template <int DQK, int DV>
 int launch_tc_bwd(const Params& p, cudaStream_t st, int* launches) {
-  return p.dropout_on ? launch_tc_bwd_t<DQK, DV, true>(p, st, launches) : launch_tc_bwd_t<DQK, DV, false>(p, st, launches);
+  if (p.H > 1)
+    return p.dropout_on ? launch_tc_bwd_t<DQK, DV, true, true>(p, st, launches)
+                        : launch_tc_bwd_t<DQK, DV, false, true>(p, st, launches);
+  return p.dropout_on ? launch_tc_bwd_t<DQK, DV, true, false>(p, st, launches)
+                      : launch_tc_bwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
 int tc_bwd_dispatch(const Params& p, cudaStream_t st, int* launches) {

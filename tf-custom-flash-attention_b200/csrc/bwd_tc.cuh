@@ -106,15 +106,15 @@ __device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols,
 template <int DA, int DB, typename Cfg>
 __device__ __forceinline__ void bwd_producer(uint8_t* smem, BwdBarriers* bars, const CUtensorMap* ra,
                                              const CUtensorMap* rb, const CUtensorMap* sa, const CUtensorMap* sb,
-                                             int res_row0, int tile0, int n, int b, const WaitCtl& ctl,
+                                             int res_row0, int tile0, int n, int hb, int ob, bool heads, const WaitCtl& ctl,
                                              uint64_t timeout_ns) {
   mbar_expect_tx(&bars->res_full, Cfg::kResA + Cfg::kResB);
 #pragma unroll
   for (int c = 0; c < DA / 64; ++c)
-    tma_load_3d(smem + Cfg::kResAOff + c * kBwdRows * 128, ra, c * 64, res_row0, b, &bars->res_full);
+    tma_load_rows(smem + Cfg::kResAOff + c * kBwdRows * 128, ra, c * 64, res_row0, hb, ob, &bars->res_full, heads);
 #pragma unroll
   for (int c = 0; c < DB / 64; ++c)
-    tma_load_3d(smem + Cfg::kResBOff + c * kBwdRows * 128, rb, c * 64, res_row0, b, &bars->res_full);
+    tma_load_rows(smem + Cfg::kResBOff + c * kBwdRows * 128, rb, c * 64, res_row0, hb, ob, &bars->res_full, heads);
   int issued = 0;
   for (int t = 0; t < n; ++t) {
     const int s = t % kBwdStages;
@@ -123,10 +123,10 @@ __device__ __forceinline__ void bwd_producer(uint8_t* smem, BwdBarriers* bars, c
     mbar_expect_tx(&bars->st_full[s], Cfg::kStA + Cfg::kStB);
 #pragma unroll
     for (int c = 0; c < DA / 64; ++c)
-      tma_load_3d(smem + Cfg::kStAOff + s * Cfg::kStA + c * kBwdTile * 128, sa, c * 64, row0, b, &bars->st_full[s]);
+      tma_load_rows(smem + Cfg::kStAOff + s * Cfg::kStA + c * kBwdTile * 128, sa, c * 64, row0, hb, ob, &bars->st_full[s], heads);
 #pragma unroll
     for (int c = 0; c < DB / 64; ++c)
-      tma_load_3d(smem + Cfg::kStBOff + s * Cfg::kStB + c * kBwdTile * 128, sb, c * 64, row0, b, &bars->st_full[s]);
+      tma_load_rows(smem + Cfg::kStBOff + s * Cfg::kStB + c * kBwdTile * 128, sb, c * 64, row0, hb, ob, &bars->st_full[s], heads);
     issued = t + 1;
   }
   if (*ctl.abort_flag) {  // let copies in flight land before the CTA exits
@@ -282,7 +282,7 @@ __device__ __forceinline__ void dq_elems(const uint32_t* sv, const uint32_t* dpv
   }
 }
 
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kBwdTcThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do, const Params p) {
@@ -292,6 +292,9 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.x % p.B;
+  // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
+  const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
+  constexpr bool heads = HEADS;
   const int64_t kt = blockIdx.x / p.B;  // low key tiles see the most causal rows: issued first
   const int64_t n0 = kt * kBwdRows;
   const int n_qtiles = static_cast<int>((p.S_q + kBwdTile - 1) / kBwdTile);
@@ -307,8 +310,8 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
 
   if (warp == 8) {
     if (lane == 0 && nq > 0)
-      bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_k, &tm_v, &tm_q, &tm_do, static_cast<int>(n0), tile0, nq,
-                                 static_cast<int>(b), ctl, p.timeout_ns);
+      bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_k, &tm_v, &tm_q, &tm_do, static_cast<int>(n0), tile0, nq, hb, ob,
+                                 heads, ctl, p.timeout_ns);
   } else if (warp == 9) {
     // Score MMAs.  S^T / dP^T of tile t go to buffer t&1, which the gradient
     // MMAs of tile t-2 read (as P~^T / dS^T): wait until those completed.
@@ -429,8 +432,8 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
     if (ok) {
       tc_fence_after();
       const bool active = j < p.S_kv;
-      __half* dv_row = static_cast<__half*>(p.dv) + (b * p.S_kv + j) * p.D_v;
-      __half* dk_row = static_cast<__half*>(p.dk) + (b * p.S_kv + j) * p.D_qk;
+      __half* dv_row = static_cast<__half*>(p.dv) + row_offset_t<HEADS>(p.H, b, j, p.S_kv, p.D_v);
+      __half* dk_row = static_cast<__half*>(p.dk) + row_offset_t<HEADS>(p.H, b, j, p.S_kv, p.D_qk);
       store_acc_row(tmem + lane_base + Cfg::kAcc0 + half * (DV / 2), DV / 64, half * (DV / 2), 1.0f, nq > 0, active,
                     dv_row, p.D_v);
       store_acc_row(tmem + lane_base + Cfg::kAcc1 + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nq > 0,
@@ -482,7 +485,7 @@ struct Dq2Barriers {
   int abort_flag;
 };
 
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kBwdTcThreads, 1)
     dq2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -494,6 +497,9 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int64_t n_qt = (p.S_q + kBwdRows - 1) / kBwdRows;
   const int64_t b = blockIdx.x % p.B;
+  // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
+  const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
+  constexpr bool heads = HEADS;
   const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
   const int64_t m0 = qt * kBwdRows;
   const int64_t n_kv_all = (p.S_kv + TN - 1) / TN;
@@ -537,12 +543,12 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
       mbar_expect_tx(&bars->res_full, Cfg::kQBytes + Cfg::kOBytes);
 #pragma unroll
       for (int c = 0; c < DQK / 64; ++c)
-        tma_load_3d(smem + Cfg::kQOff + c * kBwdRows * 128, &tm_q, c * 64, static_cast<int>(m0), static_cast<int>(b),
-                    &bars->res_full);
+        tma_load_rows(smem + Cfg::kQOff + c * kBwdRows * 128, &tm_q, c * 64, static_cast<int>(m0), hb, ob,
+                    &bars->res_full, heads);
 #pragma unroll
       for (int c = 0; c < DV / 64; ++c)
-        tma_load_3d(smem + Cfg::kOOff + c * kBwdRows * 128, &tm_do, c * 64, static_cast<int>(m0),
-                    static_cast<int>(b), &bars->res_full);
+        tma_load_rows(smem + Cfg::kOOff + c * kBwdRows * 128, &tm_do, c * 64, static_cast<int>(m0),
+                    hb, ob, &bars->res_full, heads);
       int issued = 0;
       for (int t = 0; t < nkv; ++t) {
         const int ks = t % 3, vs = t & 1;
@@ -550,14 +556,14 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
         mbar_expect_tx(&bars->k_full[ks], Cfg::kKBytes);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
-          tma_load_3d(smem + Cfg::kKOff + ks * Cfg::kKBytes + c * TN * 128, &tm_k, c * 64, t * TN,
-                      static_cast<int>(b), &bars->k_full[ks]);
+          tma_load_rows(smem + Cfg::kKOff + ks * Cfg::kKBytes + c * TN * 128, &tm_k, c * 64, t * TN,
+                      hb, ob, &bars->k_full[ks], heads);
         if (!mbar_wait(&bars->v_empty[vs], ((t >> 1) & 1) ^ 1, ctl)) break;
         mbar_expect_tx(&bars->v_full[vs], Cfg::kVBytes);
 #pragma unroll
         for (int c = 0; c < DV / 64; ++c)
-          tma_load_3d(smem + Cfg::kVOff + vs * Cfg::kVBytes + c * TN * 128, &tm_v, c * 64, t * TN,
-                      static_cast<int>(b), &bars->v_full[vs]);
+          tma_load_rows(smem + Cfg::kVOff + vs * Cfg::kVBytes + c * TN * 128, &tm_v, c * 64, t * TN,
+                      hb, ob, &bars->v_full[vs], heads);
         issued = t + 1;
       }
       if (*ctl.abort_flag) {  // let copies in flight land before the CTA exits
@@ -698,7 +704,7 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
     if (ok && nkv > 0) ok = warp_wait(&bars->acc_done, 0, ctl);
     if (ok) {
       tc_fence_after();
-      __half* dq_row = static_cast<__half*>(p.dq) + (b * p.S_q + i) * p.D_qk;
+      __half* dq_row = static_cast<__half*>(p.dq) + row_offset_t<HEADS>(p.H, b, i, p.S_q, p.D_qk);
       store_acc_row(tmem + lane_base + Cfg::kDQ + half * (DQK / 2), DQK / 64, half * (DQK / 2), p.scale, nkv > 0,
                     row_ok, dq_row, p.D_qk);
     }

@@ -26,8 +26,10 @@ struct Params {
   void* dq;
   void* dk;
   void* dv;
-  // shape
+  // shape: B folded batch rows bh = b*H + h; every [.., S, D] tensor except
+  // stats/delta is laid out [B/H, S, H, D] (H = 1: contiguous [B, S, D])
   int64_t B, S_q, S_kv;
+  int64_t H;
   int D_qk, D_v;
   // semantics
   float scale;          // as given
@@ -40,6 +42,17 @@ struct Params {
   uint64_t rng_base;    // seed + offset
   uint64_t timeout_ns;
 };
+
+// Element offset of row s of folded batch row bh in a [B/H, S, H, D] tensor.
+__host__ __device__ __forceinline__ int64_t row_offset(int64_t H, int64_t bh, int64_t s, int64_t S, int64_t D) {
+  if (H == 1) return (bh * S + s) * D;  // contiguous [B, S, D]: no division
+  return ((bh / H) * S + s) * (H * D) + (bh % H) * D;
+}
+// The same with the layout fixed at compile time (HEADS = false: H is 1).
+template <bool HEADS>
+__host__ __device__ __forceinline__ int64_t row_offset_t(int64_t H, int64_t bh, int64_t s, int64_t S, int64_t D) {
+  return HEADS ? ((bh / H) * S + s) * (H * D) + (bh % H) * D : (bh * S + s) * D;
+}
 
 template <typename T>
 __device__ __forceinline__ float to_f(T x);

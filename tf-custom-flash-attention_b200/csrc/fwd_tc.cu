@@ -11,16 +11,16 @@ using namespace sdpa_b200::host;
 namespace {
 
 // ----------------------------------------------------------------- forward
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_tc_fwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tc::FwdCfg<DQK, DV>;
-  auto kern = tc::fwd_kernel<DQK, DV, DROP>;
-  if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
+  auto kern = tc::fwd_kernel<DQK, DV, DROP, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
   CUtensorMap mq, mk, mv;
-  if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
-      !make_map_f16(&mv, p.v, p.B, p.S_kv, p.D_v, tc::kBN))
-    return SDPA_B200_ECUDA;
+  if (!make_map_f16(&mq, p.q, p.B, p.H, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.H, p.S_kv, p.D_qk, tc::kBN) ||
+      !make_map_f16(&mv, p.v, p.B, p.H, p.S_kv, p.D_v, tc::kBN))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
   const int64_t n_qt = (p.S_q + tc::kBM - 1) / tc::kBM;
   const int64_t grid = n_qt * p.B;
   if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
@@ -29,22 +29,28 @@ int launch_tc_fwd_t(const Params& p, cudaStream_t st, int* launches) {
   return launch_result();
 }
 
+template <int DQK, int DV, bool HEADS>
+int launch_tc_fwd_h(const Params& p, cudaStream_t st, int* launches) {
+  return p.dropout_on ? launch_tc_fwd_t<DQK, DV, true, HEADS>(p, st, launches)
+                      : launch_tc_fwd_t<DQK, DV, false, HEADS>(p, st, launches);
+}
+// HEADS: [B/H, S, H, D] tensors (4-D TMA maps); else contiguous [B, S, D].
 template <int DQK, int DV>
 int launch_tc_fwd(const Params& p, cudaStream_t st, int* launches) {
-  return p.dropout_on ? launch_tc_fwd_t<DQK, DV, true>(p, st, launches) : launch_tc_fwd_t<DQK, DV, false>(p, st, launches);
+  return p.H > 1 ? launch_tc_fwd_h<DQK, DV, true>(p, st, launches) : launch_tc_fwd_h<DQK, DV, false>(p, st, launches);
 }
 
 // Paired-tile forward (two 128-row query tiles per CTA).
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_pair_fwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tc::PairCfg<DQK, DV>;
-  auto kern = tc::fwd_pair_kernel<DQK, DV, DROP>;
-  if (ensure_smem(kern, Cfg::kSmemBytes, attr_done) != cudaSuccess) return SDPA_B200_ECUDA;
+  auto kern = tc::fwd_pair_kernel<DQK, DV, DROP, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
   CUtensorMap mq, mk, mv;
-  if (!make_map_f16(&mq, p.q, p.B, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.S_kv, p.D_qk, tc::kBN) ||
-      !make_map_f16(&mv, p.v, p.B, p.S_kv, p.D_v, tc::kBN))
-    return SDPA_B200_ECUDA;
+  if (!make_map_f16(&mq, p.q, p.B, p.H, p.S_q, p.D_qk, tc::kBM) || !make_map_f16(&mk, p.k, p.B, p.H, p.S_kv, p.D_qk, tc::kBN) ||
+      !make_map_f16(&mv, p.v, p.B, p.H, p.S_kv, p.D_v, tc::kBN))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
   const int64_t grid = ((p.S_q + 2 * tc::kBM - 1) / (2 * tc::kBM)) * p.B;
   if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
   kern<<<static_cast<unsigned>(grid), tc::kPairThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
@@ -57,8 +63,11 @@ int launch_pair_fwd(const Params& p, cudaStream_t st, int* launches) {
   // A single 128-row query tile per batch row leaves half of a pair idle:
   // the one-tile kernel serves those shapes.
   if (p.S_q <= tc::kBM) return launch_tc_fwd<DQK, DV>(p, st, launches);
-  return p.dropout_on ? launch_pair_fwd_t<DQK, DV, true>(p, st, launches)
-                      : launch_pair_fwd_t<DQK, DV, false>(p, st, launches);
+  if (p.H > 1)
+    return p.dropout_on ? launch_pair_fwd_t<DQK, DV, true, true>(p, st, launches)
+                        : launch_pair_fwd_t<DQK, DV, false, true>(p, st, launches);
+  return p.dropout_on ? launch_pair_fwd_t<DQK, DV, true, false>(p, st, launches)
+                      : launch_pair_fwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
 int tc_fwd_dispatch(const Params& p, cudaStream_t st, int* launches) {

@@ -85,7 +85,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
   return raw + ((1024u - (a & 1023u)) & 1023u);
 }
 
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -98,6 +98,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int64_t n_qt = (p.S_q + kBM - 1) / kBM;
   const int64_t b = blockIdx.x % p.B;
+  // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
+  const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
+  constexpr bool heads = HEADS;
   const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
   const int64_t m0 = qt * kBM;
   const int64_t n_kv_all = (p.S_kv + kBN - 1) / kBN;
@@ -139,8 +142,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_expect_tx(&bars->q_full, Cfg::kQBytes);
 #pragma unroll
       for (int c = 0; c < DQK / 64; ++c)
-        tma_load_3d(smem + Cfg::kQOff + c * kBM * 128, &tm_q, c * 64, static_cast<int>(m0), static_cast<int>(b),
-                    &bars->q_full);
+        tma_load_rows(smem + Cfg::kQOff + c * kBM * 128, &tm_q, c * 64, static_cast<int>(m0), hb, ob,
+                    &bars->q_full, heads);
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
@@ -150,11 +153,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mbar_expect_tx(&bars->k_full[s], Cfg::kKBytes);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
-          tma_load_3d(kdst + c * kBN * 128, &tm_k, c * 64, j * kBN, static_cast<int>(b), &bars->k_full[s]);
+          tma_load_rows(kdst + c * kBN * 128, &tm_k, c * 64, j * kBN, hb, ob, &bars->k_full[s], heads);
         mbar_expect_tx(&bars->v_full[s], Cfg::kVBytes);
 #pragma unroll
         for (int c = 0; c < DV / 64; ++c)
-          tma_load_3d(vdst + c * kBN * 128, &tm_v, c * 64, j * kBN, static_cast<int>(b), &bars->v_full[s]);
+          tma_load_rows(vdst + c * kBN * 128, &tm_v, c * 64, j * kBN, hb, ob, &bars->v_full[s], heads);
         issued = j + 1;
       }
       if (*ctl.abort_flag) {
@@ -344,7 +347,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const bool active = row < p.S_q;
       if (active) p.stats[b * p.S_q + row] = lse;
-      __half* orow = static_cast<__half*>(p.out) + (b * p.S_q + row) * p.D_v;
+      __half* orow = static_cast<__half*>(p.out) + row_offset_t<HEADS>(p.H, b, row, p.S_q, p.D_v);
 #pragma unroll
       for (int c = 0; c < DV / 32; ++c) {
         uint32_t o[32];
@@ -418,7 +421,7 @@ struct PairBarriers {
   int abort_flag;
 };
 
-template <int DQK, int DV, bool DROP>
+template <int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kPairThreads, 1)
     fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -431,6 +434,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   const int64_t n_pairs = (p.S_q + 2 * kBM - 1) / (2 * kBM);
   const int64_t b = blockIdx.x % p.B;
+  // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
+  const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
+  constexpr bool heads = HEADS;
   const int64_t pq = n_pairs - 1 - blockIdx.x / p.B;  // longest causal rows first
   const int64_t m0 = pq * 2 * kBM;
   const int64_t n_kv_all = (p.S_kv + kBN - 1) / kBN;
@@ -474,8 +480,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
-          tma_load_3d(smem + Cfg::kQOff + t * Cfg::kQBytes + c * kBM * 128, &tm_q, c * 64,
-                      static_cast<int>(m0 + t * kBM), static_cast<int>(b), &bars->q_full);
+          tma_load_rows(smem + Cfg::kQOff + t * Cfg::kQBytes + c * kBM * 128, &tm_q, c * 64,
+                      static_cast<int>(m0 + t * kBM), hb, ob, &bars->q_full, heads);
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
@@ -485,11 +491,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         mbar_expect_tx(&bars->k_full[s], Cfg::kKBytes);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
-          tma_load_3d(kdst + c * kBN * 128, &tm_k, c * 64, j * kBN, static_cast<int>(b), &bars->k_full[s]);
+          tma_load_rows(kdst + c * kBN * 128, &tm_k, c * 64, j * kBN, hb, ob, &bars->k_full[s], heads);
         mbar_expect_tx(&bars->v_full[s], Cfg::kVBytes);
 #pragma unroll
         for (int c = 0; c < DV / 64; ++c)
-          tma_load_3d(vdst + c * kBN * 128, &tm_v, c * 64, j * kBN, static_cast<int>(b), &bars->v_full[s]);
+          tma_load_rows(vdst + c * kBN * 128, &tm_v, c * 64, j * kBN, hb, ob, &bars->v_full[s], heads);
         issued = j + 1;
       }
       if (*ctl.abort_flag) {  // let copies in flight land before the CTA exits
@@ -696,7 +702,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       const bool active = row < p.S_q;
       if (active) p.stats[b * p.S_q + row] = lse;
-      __half* orow = static_cast<__half*>(p.out) + (b * p.S_q + row) * p.D_v;
+      __half* orow = static_cast<__half*>(p.out) + row_offset_t<HEADS>(p.H, b, row, p.S_q, p.D_v);
 #pragma unroll
       for (int c = 0; c < DV / 32; ++c) {
         uint32_t o[32];

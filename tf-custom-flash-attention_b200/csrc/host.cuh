@@ -6,6 +6,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdio>
 #include <mutex>
 
 #include "../../include/sdpa_b200.h"
@@ -24,6 +25,20 @@ inline int dmax_bucket(int64_t d) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Detail of the last SDPA_B200_ECUDA returned on this thread (sdpa_b200_last_error_detail).
+inline thread_local char t_err_detail[160] = "";
+inline int cuda_failure(const char* what, int code, const char* name) {
+  std::snprintf(t_err_detail, sizeof(t_err_detail), "%s: %s (%d)", what, name ? name : "?", code);
+  return SDPA_B200_ECUDA;
+}
+inline int cuda_failure(const char* what, cudaError_t e) {
+  return cuda_failure(what, static_cast<int>(e), cudaGetErrorName(e));
+}
+inline bool map_failure(int code, const char* name) {
+  cuda_failure("TMA descriptor", code, name);
+  return false;
+}
+
 // ---------------------------------------------------------------- TMA maps
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -39,19 +54,35 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [B, S, D] fp16 tensor, box = 64 columns x `rows` rows x 1 batch, 128B swizzle.
-// Columns beyond D and rows beyond S read as zero.
-inline bool make_map_f16(CUtensorMap* m, const void* base, int64_t B, int64_t S, int64_t D, int rows) {
+// fp16 tensor [B/H, S, H, D] as a 4-D map over (column, head, row, outer
+// batch), box = 64 columns x 1 head x `rows` rows x 1; for H = 1 (contiguous
+// [B, S, D]) the 3-D map (column, row, batch), box 64 x `rows` x 1.  128B
+// swizzle; the shared-memory tile is the same either way.  Columns beyond D
+// and rows beyond S read as zero.  Failures record their detail.
+inline bool make_map_f16(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S, int64_t D, int rows) {
   auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(rows), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  if (!fn) return map_failure(0, "cuTensorMapEncodeTiled unavailable");
+  if (H < 1 || B % H != 0) return map_failure(static_cast<int>(H), "bad head count");
+  if (H == 1) {  // contiguous [B, S, D]: the 3-D map (column, row, batch)
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
+  }
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(B / H)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(H * D * 2),
+                           static_cast<cuuint64_t>(S * H * D * 2)};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
 }
 
 // Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
@@ -69,7 +100,7 @@ inline cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& do
 
 inline int launch_result() {
   const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SDPA_B200_OK : SDPA_B200_ECUDA;
+  return e == cudaSuccess ? SDPA_B200_OK : cuda_failure("kernel launch", e);
 }
 
 }  // namespace host

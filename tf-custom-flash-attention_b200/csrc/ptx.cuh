@@ -92,6 +92,26 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, int
       : "memory");
 }
 
+// 4-D tiled load (coordinates x, y, z, w innermost first); same rule for x.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+// Rows [row, row + box) of folded batch row (head h, outer batch bo) of a map
+// made by make_map_f16: with heads, 4-D coordinates (column x, head, row,
+// outer batch); without (H = 1), the 3-D map (column x, row, batch).
+__device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* m, int x, int row, int h, int bo,
+                                              uint64_t* bar, bool heads) {
+  if (heads)
+    tma_load_4d(dst, m, x, h, row, bo, bar);
+  else
+    tma_load_3d(dst, m, x, row, bo, bar);
+}
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

@@ -19,13 +19,13 @@ constexpr int kBwdRows = 64;   // rows owned per CTA in dkdv / dq
 constexpr int kBwdTile = 32;   // rows per staged tile of the other side
 
 template <typename T>
-__device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t row0, int64_t nrows_total, int rows,
-                                           int D, int DM, int tid, int nthreads) {
-  // dst[r][d] (row-major, width DM) <- src rows row0.. (zero outside)
+__device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t ld, int64_t row0, int64_t nrows_total,
+                                           int rows, int D, int DM, int tid, int nthreads) {
+  // dst[r][d] (row-major, width DM) <- src rows row0.. (row stride ld; zero outside)
   for (int idx = tid; idx < rows * DM; idx += nthreads) {
     int r = idx / DM, d = idx - r * DM;
     int64_t gr = row0 + r;
-    dst[idx] = (gr < nrows_total && d < D) ? to_f<T>(src[gr * D + d]) : 0.0f;
+    dst[idx] = (gr < nrows_total && d < D) ? to_f<T>(src[gr * ld + d]) : 0.0f;
   }
 }
 
@@ -39,14 +39,16 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
   const int tid = threadIdx.x;
   const int64_t row = qt * kFwdRows + tid;
   const bool active = row < p.S_q;
-  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
-  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
-  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
+  // rows of folded batch row b; row strides H*D ([B/H, S, H, D] layout)
+  const T* Q = static_cast<const T*>(p.q) + row_offset(p.H, b, 0, p.S_q, p.D_qk);
+  const T* K = static_cast<const T*>(p.k) + row_offset(p.H, b, 0, p.S_kv, p.D_qk);
+  const T* V = static_cast<const T*>(p.v) + row_offset(p.H, b, 0, p.S_kv, p.D_v);
+  const int64_t ldqk = p.H * p.D_qk, ldv = p.H * p.D_v;
 
   float qr[DM], acc[DM];
 #pragma unroll
   for (int d = 0; d < DM; ++d) {
-    qr[d] = (active && d < p.D_qk) ? to_f<T>(Q[row * p.D_qk + d]) * p.scale_log2 : 0.0f;
+    qr[d] = (active && d < p.D_qk) ? to_f<T>(Q[row * ldqk + d]) * p.scale_log2 : 0.0f;
     acc[d] = 0.0f;
   }
   float m = -INFINITY, l = 0.0f;
@@ -55,8 +57,8 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
   if (p.causal) kv_end = min(p.S_kv, (qt + 1) * kFwdRows);
   for (int64_t kv0 = 0; kv0 < kv_end; kv0 += kFwdKeys) {
     __syncthreads();
-    stage_rows<T>(Ks, K, kv0, p.S_kv, kFwdKeys, p.D_qk, DM, tid, kFwdRows);
-    stage_rows<T>(Vs, V, kv0, p.S_kv, kFwdKeys, p.D_v, DM, tid, kFwdRows);
+    stage_rows<T>(Ks, K, ldqk, kv0, p.S_kv, kFwdKeys, p.D_qk, DM, tid, kFwdRows);
+    stage_rows<T>(Vs, V, ldv, kv0, p.S_kv, kFwdKeys, p.D_v, DM, tid, kFwdRows);
     __syncthreads();
     if (!active) continue;
     float sc[kFwdKeys];
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
   const float lse = (m == -INFINITY) ? kNegInit + logf(kEps) : m * kLn2 + logf(l + kEps);
   p.stats[orow] = lse;
   const float inv = (l > kEps) ? p.dp_inv / l : 0.0f;
-  T* O = static_cast<T*>(p.out) + orow * p.D_v;
+  T* O = static_cast<T*>(p.out) + row_offset(p.H, b, row, p.S_q, p.D_v);
 #pragma unroll
   for (int d = 0; d < DM; ++d)
     if (d < p.D_v) O[d] = from_f<T>(acc[d] * inv);
@@ -104,8 +106,9 @@ __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= p.B * p.S_q) return;
-  const T* dO = static_cast<const T*>(p.d_o) + row * p.D_v;
-  const T* O = static_cast<const T*>(p.o) + row * p.D_v;
+  const int64_t off = p.H == 1 ? row * p.D_v : row_offset(p.H, row / p.S_q, row % p.S_q, p.S_q, p.D_v);
+  const T* dO = static_cast<const T*>(p.d_o) + off;
+  const T* O = static_cast<const T*>(p.o) + off;
   float s = 0.0f;
   for (int d = lane; d < p.D_v; d += 32) s = fmaf(to_f<T>(dO[d]), to_f<T>(O[d]), s);
 #pragma unroll
@@ -161,15 +164,17 @@ __global__ void __launch_bounds__(kBwdRows * dkdv_split<DM>()) dkdv_kernel(Param
   const int r = tid / SPLIT, h = tid % SPLIT, d0 = h * DH;
   const int64_t kv = kt * kBwdRows + r;
   const bool active = kv < p.S_kv;
-  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
-  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
-  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
-  const T* dO = static_cast<const T*>(p.d_o) + b * p.S_q * p.D_v;
+  // rows of folded batch row b; row strides H*D ([B/H, S, H, D] layout)
+  const T* Q = static_cast<const T*>(p.q) + row_offset(p.H, b, 0, p.S_q, p.D_qk);
+  const T* K = static_cast<const T*>(p.k) + row_offset(p.H, b, 0, p.S_kv, p.D_qk);
+  const T* V = static_cast<const T*>(p.v) + row_offset(p.H, b, 0, p.S_kv, p.D_v);
+  const int64_t ldqk = p.H * p.D_qk, ldv = p.H * p.D_v;
+  const T* dO = static_cast<const T*>(p.d_o) + row_offset(p.H, b, 0, p.S_q, p.D_v);
   for (int idx = tid; idx < DM * kBwdRows; idx += NT) {
     const int d = idx / kBwdRows, rr = idx - d * kBwdRows;
     const int64_t kvr = kt * kBwdRows + rr;
-    Kt[idx] = (kvr < p.S_kv && d < p.D_qk) ? to_f<T>(K[kvr * p.D_qk + d]) : 0.0f;
-    Vt[idx] = (kvr < p.S_kv && d < p.D_v) ? to_f<T>(V[kvr * p.D_v + d]) : 0.0f;
+    Kt[idx] = (kvr < p.S_kv && d < p.D_qk) ? to_f<T>(K[kvr * ldqk + d]) : 0.0f;
+    Vt[idx] = (kvr < p.S_kv && d < p.D_v) ? to_f<T>(V[kvr * ldv + d]) : 0.0f;
   }
   float dk[DH], dv[DH];
 #pragma unroll
@@ -177,8 +182,8 @@ __global__ void __launch_bounds__(kBwdRows * dkdv_split<DM>()) dkdv_kernel(Param
   const int64_t q_start = p.causal ? (kt * kBwdRows / kBwdTile) * kBwdTile : 0;
   for (int64_t q0 = q_start; q0 < p.S_q; q0 += kBwdTile) {
     __syncthreads();
-    stage_rows<T>(Qs, Q, q0, p.S_q, kBwdTile, p.D_qk, DM, tid, NT);
-    stage_rows<T>(dOs, dO, q0, p.S_q, kBwdTile, p.D_v, DM, tid, NT);
+    stage_rows<T>(Qs, Q, ldqk, q0, p.S_q, kBwdTile, p.D_qk, DM, tid, NT);
+    stage_rows<T>(dOs, dO, ldv, q0, p.S_q, kBwdTile, p.D_v, DM, tid, NT);
     for (int rr = tid; rr < kBwdTile; rr += NT) {
       const int64_t i = q0 + rr;
       lse_s[rr] = i < p.S_q ? p.lse[b * p.S_q + i] * kLog2e : 0.0f;
@@ -215,8 +220,8 @@ __global__ void __launch_bounds__(kBwdRows * dkdv_split<DM>()) dkdv_kernel(Param
     }
   }
   if (!active) return;
-  T* dK = static_cast<T*>(p.dk) + (b * p.S_kv + kv) * p.D_qk;
-  T* dV = static_cast<T*>(p.dv) + (b * p.S_kv + kv) * p.D_v;
+  T* dK = static_cast<T*>(p.dk) + row_offset(p.H, b, kv, p.S_kv, p.D_qk);
+  T* dV = static_cast<T*>(p.dv) + row_offset(p.H, b, kv, p.S_kv, p.D_v);
 #pragma unroll
   for (int d = 0; d < DH; ++d) {
     if (d0 + d < p.D_qk) dK[d0 + d] = from_f<T>(dk[d]);
@@ -237,13 +242,15 @@ __global__ void __launch_bounds__(kBwdRows) dq_kernel(Params p) {
   const int tid = threadIdx.x;
   const int64_t row = qt * kBwdRows + tid;
   const bool active = row < p.S_q;
-  const T* Q = static_cast<const T*>(p.q) + b * p.S_q * p.D_qk;
-  const T* K = static_cast<const T*>(p.k) + b * p.S_kv * p.D_qk;
-  const T* V = static_cast<const T*>(p.v) + b * p.S_kv * p.D_v;
-  const T* dO = static_cast<const T*>(p.d_o) + b * p.S_q * p.D_v;
+  // rows of folded batch row b; row strides H*D ([B/H, S, H, D] layout)
+  const T* Q = static_cast<const T*>(p.q) + row_offset(p.H, b, 0, p.S_q, p.D_qk);
+  const T* K = static_cast<const T*>(p.k) + row_offset(p.H, b, 0, p.S_kv, p.D_qk);
+  const T* V = static_cast<const T*>(p.v) + row_offset(p.H, b, 0, p.S_kv, p.D_v);
+  const int64_t ldqk = p.H * p.D_qk, ldv = p.H * p.D_v;
+  const T* dO = static_cast<const T*>(p.d_o) + row_offset(p.H, b, 0, p.S_q, p.D_v);
   for (int d = 0; d < DM; ++d) {
-    Qt[d * kBwdRows + tid] = (active && d < p.D_qk) ? to_f<T>(Q[row * p.D_qk + d]) : 0.0f;
-    dOt[d * kBwdRows + tid] = (active && d < p.D_v) ? to_f<T>(dO[row * p.D_v + d]) : 0.0f;
+    Qt[d * kBwdRows + tid] = (active && d < p.D_qk) ? to_f<T>(Q[row * ldqk + d]) : 0.0f;
+    dOt[d * kBwdRows + tid] = (active && d < p.D_v) ? to_f<T>(dO[row * ldv + d]) : 0.0f;
   }
   const float lse2 = active ? p.lse[b * p.S_q + row] * kLog2e : 0.0f;
   const float delta = active ? p.delta[b * p.S_q + row] : 0.0f;
@@ -255,8 +262,8 @@ __global__ void __launch_bounds__(kBwdRows) dq_kernel(Params p) {
   if (p.causal) kv_end = min(p.S_kv, (qt + 1) * kBwdRows);
   for (int64_t kv0 = 0; kv0 < kv_end; kv0 += kBwdTile) {
     __syncthreads();
-    stage_rows<T>(Ks, K, kv0, p.S_kv, kBwdTile, p.D_qk, DM, tid, kBwdRows);
-    stage_rows<T>(Vs, V, kv0, p.S_kv, kBwdTile, p.D_v, DM, tid, kBwdRows);
+    stage_rows<T>(Ks, K, ldqk, kv0, p.S_kv, kBwdTile, p.D_qk, DM, tid, kBwdRows);
+    stage_rows<T>(Vs, V, ldv, kv0, p.S_kv, kBwdTile, p.D_v, DM, tid, kBwdRows);
     __syncthreads();
     if (!active) continue;
     for (int jj = 0; jj < kBwdTile; ++jj) {
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kBwdRows) dq_kernel(Params p) {
     }
   }
   if (!active) return;
-  T* dQ = static_cast<T*>(p.dq) + (b * p.S_q + row) * p.D_qk;
+  T* dQ = static_cast<T*>(p.dq) + row_offset(p.H, b, row, p.S_q, p.D_qk);
 #pragma unroll
   for (int d = 0; d < DM; ++d)
     if (d < p.D_qk) dQ[d] = from_f<T>(dq[d]);

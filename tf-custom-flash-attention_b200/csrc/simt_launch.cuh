@@ -40,8 +40,8 @@ int launch_simt_bwd(const Params& p, cudaStream_t st, int* launches) {
     if (int r = launch_result()) return r;
   }
   const size_t smkv = simt::dkdv_smem<DM>(), smq = simt::dq_smem<DM>();
-  if (ensure_smem(simt::dkdv_kernel<T, DM>, smkv, attr_kv) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (ensure_smem(simt::dq_kernel<T, DM>, smq, attr_q) != cudaSuccess) return SDPA_B200_ECUDA;
+  if (cudaError_t e = ensure_smem(simt::dkdv_kernel<T, DM>, smkv, attr_kv)) return cuda_failure("shared-memory attribute", e);
+  if (cudaError_t e = ensure_smem(simt::dq_kernel<T, DM>, smq, attr_q)) return cuda_failure("shared-memory attribute", e);
   const int64_t gkv = ((p.S_kv + simt::kBwdRows - 1) / simt::kBwdRows) * p.B;
   const int64_t gq = ((p.S_q + simt::kBwdRows - 1) / simt::kBwdRows) * p.B;
   if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;

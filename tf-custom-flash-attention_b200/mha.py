@@ -6,6 +6,12 @@ axis with heads innermost (so the dropout counter of folded row b*H + h is the
 reference's), `scale = 1/sqrt(head_dim)`, and while training the dropout
 offset advances by B*H*S_q*S_kv per call (mha.py:162-165) so successive steps
 draw fresh masks; evaluation uses dropout 0 and offset 0 (mha.py:150-155).
+
+Where the sequence axis is second to last and the feature axis last (the usual
+[..., S, d_model]), splitting the features into heads is a free view
+[B, S, H, Dh] and the layer calls the head-strided kernels (autograd.sdpa_bshd)
+directly: no transposes in either direction.  Other axis orders take the
+transposing path above.  Both give the same results and dropout masks.
 """
 from __future__ import annotations
 
@@ -47,11 +53,31 @@ class MHA(torch.nn.Module):
         bshape = x.shape[:-3]
         return x.reshape(-1, x.shape[-2], x.shape[-1]).contiguous(), bshape, head_dim
 
+    def _forward_strided(self, q, k, v):
+        """[..., S, H*Dh] inputs viewed as [B, S, H, Dh]: no copies."""
+        def view(x):
+            if x.shape[-1] % self.num_heads:
+                raise ValueError(f"num_heads {self.num_heads} does not divide the feature size {x.shape[-1]}")
+            x = x.contiguous()
+            return x.reshape(-1, x.shape[-2], self.num_heads, x.shape[-1] // self.num_heads)
+        q4, k4, v4 = view(q), view(k), view(v)
+        scale = 1.0 / float(q4.shape[-1]) ** 0.5
+        if self.training:
+            dropout, offset = self.dropout, self.offset
+        else:
+            dropout, offset = 0.0, 0
+        o4 = autograd.sdpa_bshd(q4, k4, v4, self.seed, offset, dropout, scale, self.causal_mask)
+        if self.training:
+            self.offset = sharding.advance_offset(self.offset, q4.shape[0] * self.num_heads, q4.shape[1], k4.shape[1])
+        return o4.reshape(*q.shape[:-1], o4.shape[2] * o4.shape[3])
+
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         if not (q.dim() == k.dim() == v.dim()):
             raise ValueError("q, k, v should have the same rank")
         rank = q.dim()
         s_ax, f_ax = self._axes(rank)
+        if s_ax == rank - 2 and f_ax == rank - 1 and q.shape[:-2] == k.shape[:-2] == v.shape[:-2]:
+            return self._forward_strided(q, k, v)
         q3, bshape, head_dim = self._split(q, s_ax, f_ax)
         k3, _, _ = self._split(k, s_ax, f_ax)
         v3, _, head_dim_v = self._split(v, s_ax, f_ax)

@@ -61,7 +61,8 @@ def _check(rc: int):
         return
     if rc in (_lib.EINVAL, _lib.EUNSUPPORTED, _lib.EWORKSPACE):
         raise InvalidArgumentError(_lib.strerror(rc))
-    raise KernelError(_lib.strerror(rc))
+    detail = _lib.lib().sdpa_b200_last_error_detail().decode() if rc == _lib.ECUDA else ""
+    raise KernelError(_lib.strerror(rc) + (f" [{detail}]" if detail else ""))
 
 
 _FEATURE_MSG = ("CUDA kernel does not support feature size over 128. Set smaller feature size or use more heads")
@@ -170,6 +171,81 @@ def sdpa_grad(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale
     return dq, dk, dv
 
 
+def _bshd_dims(q, k, v):
+    for i, t in enumerate((q, k, v)):
+        if t.dim() != 4:
+            raise InvalidArgumentError(f"Shape must be rank 4 ([B, S, H, D]) but is rank {t.dim()} for input {i}")
+    B, S_q, H, D_qk = q.shape
+    S_kv, D_v = k.shape[1], v.shape[3]
+    if k.shape[0] != B or v.shape[0] != B:
+        raise InvalidArgumentError("K/V batch size mismatch")
+    if k.shape[2] != H or v.shape[2] != H:
+        raise InvalidArgumentError("K/V head count mismatch")
+    if k.shape[3] != D_qk:
+        raise InvalidArgumentError("K feature size mismatch")
+    if v.shape[1] != S_kv:
+        raise InvalidArgumentError("V seq size mismatch")
+    if max(D_qk, D_v) > 128:
+        raise InvalidArgumentError(_FEATURE_MSG)
+    return B, H, S_q, S_kv, D_qk, D_v
+
+
+def sdpa_bshd(q, k, v, seed, offset, scale: float = 1.0, dropout: float = 0.0, causal_mask: bool = False):
+    """Attention over head-strided tensors (extension for the MHA layer, no reference op).
+
+    q [B,S_q,H,D_qk], k [B,S_kv,H,D_qk], v [B,S_kv,H,D_v] -> (output [B,S_q,H,D_v],
+    stats [B,H,S_q] float32), read and written in place.  Equal to ``sdpa`` on the
+    [B*H,S,D] tensors mha.py:103-129 builds by transposing (heads innermost in the
+    folded batch index, so the dropout masks agree too)."""
+    B, H, S_q, S_kv, D_qk, D_v = _bshd_dims(q, k, v)
+    if causal_mask and S_q != S_kv:
+        raise InvalidArgumentError("seq size Q != K while causal_mask = True")
+    (q, k, v), dt = _prep([q, k, v])
+    out = torch.empty((B, S_q, H, D_v), dtype=q.dtype, device=q.device)
+    stats = torch.empty((B, H, S_q), dtype=torch.float32, device=q.device)
+    if B * H * S_q == 0:
+        return out, stats
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream().cuda_stream
+        rc = _lib.lib().sdpa_b200_fwd_bshd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                           stats.data_ptr(), B, H, S_q, S_kv, D_qk, D_v, float(scale),
+                                           float(dropout), int(bool(causal_mask)), _scalar_u64(seed, "seed"),
+                                           _scalar_u64(offset, "offset"), st)
+    _check(rc)
+    return out, stats
+
+
+def sdpa_grad_bshd(q, k, v, out, stats, do, seed, offset, dropout: float = 0.0, scale: float = 1.0,
+                   causal_mask: bool = False, *, d_stats=None):
+    """Gradients (dq, dk, dv) of ``sdpa_bshd``, shaped like (q, k, v) ([B,S,H,D])."""
+    B, H, S_q, S_kv, D_qk, D_v = _bshd_dims(q, k, v)
+    if tuple(out.shape) != (B, S_q, H, D_v) or tuple(do.shape) != (B, S_q, H, D_v):
+        raise InvalidArgumentError("O / dO must be [B, S_q, H, D_v]")
+    if tuple(stats.shape) != (B, H, S_q) or stats.dtype != torch.float32:
+        raise InvalidArgumentError("stats must be float32 [B, H, S_q]")
+    if causal_mask and S_q != S_kv:
+        raise InvalidArgumentError("seq size Q != K while causal_mask = True")
+    (q, k, v, out, do), dt = _prep([q, k, v, out, do])
+    stats = stats.contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if d_stats is not None:
+        d_stats = d_stats.to(torch.float32).contiguous()
+        if tuple(d_stats.shape) != (B, H, S_q):
+            raise InvalidArgumentError("d_stats must be [B, H, S_q]")
+    L = _lib.lib()
+    ws_bytes = L.sdpa_b200_bwd_workspace_bytes(dt, B * H, S_q, S_kv, D_qk, D_v)
+    ws = torch.empty((max(ws_bytes, 4) + 3) // 4, dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream().cuda_stream
+        rc = L.sdpa_b200_bwd_bshd(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), stats.data_ptr(),
+                                  d_stats.data_ptr() if d_stats is not None else None, do.data_ptr(),
+                                  dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, H, S_q, S_kv, D_qk, D_v,
+                                  float(scale), float(dropout), int(bool(causal_mask)), _scalar_u64(seed, "seed"),
+                                  _scalar_u64(offset, "offset"), ws.data_ptr(), ws_bytes, st)
+    _check(rc)
+    return dq, dk, dv
+
+
 def dropout_mask(seed, offset, B: int, S_q: int, S_kv: int, dropout: float, device=None) -> torch.Tensor:
     """uint8 [B,S_q,S_kv], 1 where the kernels drop (b,i,j): the device RNG itself."""
     m = torch.empty((B, S_q, S_kv), dtype=torch.uint8, device=device or "cuda")
@@ -186,7 +262,7 @@ def device_status(device=None) -> int:
     with torch.cuda.device(device or torch.cuda.current_device()):
         rc = _lib.lib().sdpa_b200_device_status(ctypes.byref(w), torch.cuda.current_stream().cuda_stream)
     if rc not in (_lib.OK, _lib.ETIMEOUT):
-        raise KernelError(_lib.strerror(rc))
+        _check(rc)
     return int(w.value)
 
 
