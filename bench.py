@@ -265,7 +265,7 @@ def run_ours(args, w):
     kernel_ms = None
     if per_kernel and len(kev) == args.steps:
         kernel_ms = {name: sum(e[i].elapsed_time(e[i + 1]) for e in kev) / args.steps
-                     for i, name in enumerate(("delta", "dkdv", "dq"))}
+                     for i, name in enumerate(("dq", "dkdv"))}
     clk = clocks.stop()
     per_rank = [{"rank": rank, "ms_per_step": total_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
                  "reasons": clk.get("reasons")}]

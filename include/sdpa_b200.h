@@ -152,10 +152,11 @@ int sdpa_b200_bwd_noalloc(int dtype, const void* q, const void* k, const void* v
                           int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout,
                           int causal, uint64_t seed, uint64_t offset, void* stream);
 
-/* Diagnostic: when events != NULL, the next backward calls on this host
- * thread record events[0..3] (cudaEvent_t) on their stream before the rowsum
- * kernel, before the dK/dV kernel, before the dQ kernel and after it, so a
- * caller can time each kernel.  n must be 4; NULL turns it off. */
+/* Diagnostic: when events != NULL, the next tensor-core backward calls on
+ * this host thread record events[0..3] (cudaEvent_t) on their stream before
+ * the dQ kernel (which also computes the rowsum D), before the dK/dV kernel,
+ * and after it (events[2] and [3] both), so a caller can time each kernel.
+ * n must be 4; NULL turns it off. */
 int sdpa_b200_set_bwd_events(void* const* events, int n);
 
 /* ABI version (major*100 + minor). */

@@ -9,7 +9,7 @@ using namespace sdpa_b200::host;
 
 namespace {
 
-// tcgen05 backward: delta (rowsum dO*O) -> dK/dV kernel -> dQ kernel.
+// tcgen05 backward: dQ kernel (which also writes D = rowsum(dO*O)) -> dK/dV kernel.
 template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
@@ -27,21 +27,19 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
       !make_map_f16(&q128, p.q, p.B, p.H, p.S_q, p.D_qk, tc::kBwdRows) ||
       !make_map_f16(&do128, p.d_o, p.B, p.H, p.S_q, p.D_v, tc::kBwdRows))
     return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
-  const int64_t rows = p.B * p.S_q;
-  sdpa_b200::record_bwd_event(0, st);
-  simt::delta_kernel<__half><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
-  ++*launches;
-  if (int r = launch_result()) return r;
   const int64_t gkv = ((p.S_kv + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
   const int64_t gq = ((p.S_q + tc::kBwdRows - 1) / tc::kBwdRows) * p.B;
   if (gkv > 0x7fffffffLL || gq > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  // dQ first: it also computes D = rowsum(dO * O) (into the workspace), which
+  // the dK/dV kernel reads.
+  sdpa_b200::record_bwd_event(0, st);
+  kq<<<static_cast<unsigned>(gq), tc::kBwdTcThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
+  ++*launches;
+  if (int r = launch_result()) return r;
   sdpa_b200::record_bwd_event(1, st);
   kkv<<<static_cast<unsigned>(gkv), tc::kBwdTcThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
   ++*launches;
-  if (int r = launch_result()) return r;
   sdpa_b200::record_bwd_event(2, st);
-  kq<<<static_cast<unsigned>(gq), tc::kBwdTcThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
-  ++*launches;
   sdpa_b200::record_bwd_event(3, st);
   return launch_result();
 }

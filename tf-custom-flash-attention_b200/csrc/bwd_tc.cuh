@@ -654,11 +654,48 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
     const int64_t iw0 = m0 + (warp & 3) * 32;
     const bool row_ok = i < p.S_q;
     const float lse2 = row_ok ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;
-    const float delta = row_ok ? p.delta[b * p.S_q + i] : 0.0f;
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
     const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
     const uint64_t rbase = p.rng_base + static_cast<uint64_t>(b * p.S_q + i) * static_cast<uint64_t>(p.S_kv);
-    bool ok = true;
+    // D_i = sum_d dO[i,d] O[i,d] (minus the stats gradient, when given) of this
+    // CTA's rows, from the resident dO tile (128B-swizzled: 16-byte chunk k of
+    // row r at r*128 + ((k ^ (r & 7)) << 4) in box k/8) and O in global
+    // memory; both threads of a row compute the whole sum (no exchange), the
+    // first writes it for the dK/dV kernel, which runs after this one.  The O
+    // row is loaded before the resident tiles arrive, so its latency overlaps
+    // theirs.
+    uint4 orow_v[DV / 8];
+    if (row_ok) {
+      const __half* orow = static_cast<const __half*>(p.o) + row_offset_t<HEADS>(p.H, b, i, p.S_q, p.D_v);
+#pragma unroll
+      for (int g = 0; g < DV / 8; ++g)
+        orow_v[g] = g * 8 < p.D_v ? *reinterpret_cast<const uint4*>(orow + g * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    bool ok = warp_wait(&bars->res_full, 0, ctl);
+    float delta = 0.0f;
+    if (ok && row_ok) {
+      const uint8_t* dO_s = smem + Cfg::kOOff;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int g = 0; g < DV / 8; ++g) {
+        const uint4 ov = orow_v[g];
+        const uint4 dv = *reinterpret_cast<const uint4*>(dO_s + (g >> 3) * (kBwdRows * 128) + r * 128 +
+                                                           (((g & 7) ^ (r & 7)) << 4));
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 of = __half22float2(*reinterpret_cast<const __half2*>(&ow[e]));
+          const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dw[e]));
+          acc[e] = fmaf(df.x, of.x, acc[e]);
+          acc[e] = fmaf(df.y, of.y, acc[e]);
+        }
+      }
+      delta = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      // A gradient g_i reaching stats_i = logsumexp adds g_i * p_ij to dS_ij,
+      // i.e. it enters dS = p (dP - D) as D - g.
+      if (p.d_stats) delta -= p.d_stats[b * p.S_q + i];
+      if (half == 0) p.delta[b * p.S_q + i] = delta;
+    }
     for (int t = 0; t < nkv; ++t) {
       if (!warp_wait(&bars->s_full, t & 1, ctl)) {
         ok = false;
