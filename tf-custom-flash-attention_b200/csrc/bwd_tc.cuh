@@ -68,7 +68,8 @@ struct BwdBarriers {
   uint64_t vec_ready[2];
   uint64_t acc_done;
   uint64_t mma_done;
-  uint64_t g_done[2];    // dK/dV kernel: gradient MMAs of the tile in S/dP buffer sb completed
+  uint64_t gv_done[2];   // dK/dV kernel: dV MMAs of the tile in buffer sb completed (P~^T read)
+  uint64_t gk_done[2];   // dK/dV kernel: dK MMAs of the tile in buffer sb completed (dS^T read)
   uint64_t mma_done2;    // dK/dV kernel: drain of the second issuing thread
   uint32_t tmem_base;
   int abort_flag;
@@ -89,8 +90,10 @@ __device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols,
     }
     mbar_init(&bars->acc_done, 1);
     mbar_init(&bars->mma_done, 1);
-    mbar_init(&bars->g_done[0], 1);
-    mbar_init(&bars->g_done[1], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->gv_done[s], 1);
+      mbar_init(&bars->gk_done[s], 1);
+    }
     mbar_init(&bars->mma_done2, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -140,24 +143,17 @@ __device__ __forceinline__ void bwd_producer(uint8_t* smem, BwdBarriers* bars, c
   }
 }
 
-// 128 x 64 score tiles of both kernels: X[sb] = resA * stA^T (K = DA) and
-// Y[sb] = resB * stB^T (K = DB), both operands K-major.
-template <int DA, int DB, typename Cfg>
-__device__ __forceinline__ void bwd_issue_scores(uint32_t tmem, uint32_t smem_base, int s, int sb) {
+// One of the two score products of the dK/dV kernel: TMEM columns OUT + sb*64
+// (+)= resident (at smem RES) * stage tile (at smem ST + s*STB)^T, K = D.
+template <int D, typename Cfg, uint32_t OUT, uint32_t RES, uint32_t ST, uint32_t STB>
+__device__ __forceinline__ void bwd_issue_scores_half(uint32_t tmem, uint32_t smem_base, int s, int sb) {
   constexpr uint32_t idesc = make_idesc(kBwdRows, kBwdTile, false, false, false);
-  const uint32_t ra = smem_base + Cfg::kResAOff, rb = smem_base + Cfg::kResBOff;
-  const uint32_t sa = smem_base + Cfg::kStAOff + s * Cfg::kStA, sbb = smem_base + Cfg::kStBOff + s * Cfg::kStB;
+  const uint32_t ra = smem_base + RES, sa = smem_base + ST + s * STB;
 #pragma unroll
-  for (int kk = 0; kk < DA / 16; ++kk) {
+  for (int kk = 0; kk < D / 16; ++kk) {
     const uint64_t a = make_sw128_desc(ra + (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32, 16, 1024);
     const uint64_t bb = make_sw128_desc(sa + (kk >> 2) * (kBwdTile * 128) + (kk & 3) * 32, 16, 1024);
-    mma_f16_ss(tmem + Cfg::kS + sb * kBwdTile, a, bb, idesc, kk > 0 ? 1u : 0u);
-  }
-#pragma unroll
-  for (int kk = 0; kk < DB / 16; ++kk) {
-    const uint64_t a = make_sw128_desc(rb + (kk >> 2) * (kBwdRows * 128) + (kk & 3) * 32, 16, 1024);
-    const uint64_t bb = make_sw128_desc(sbb + (kk >> 2) * (kBwdTile * 128) + (kk & 3) * 32, 16, 1024);
-    mma_f16_ss(tmem + Cfg::kDP + sb * kBwdTile, a, bb, idesc, kk > 0 ? 1u : 0u);
+    mma_f16_ss(tmem + OUT + sb * kBwdTile, a, bb, idesc, kk > 0 ? 1u : 0u);
   }
 }
 
@@ -313,19 +309,27 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
       bwd_producer<DQK, DV, Cfg>(smem, bars, &tm_k, &tm_v, &tm_q, &tm_do, static_cast<int>(n0), tile0, nq, hb, ob,
                                  heads, ctl, p.timeout_ns);
   } else if (warp == 9) {
-    // Score MMAs.  S^T / dP^T of tile t go to buffer t&1, which the gradient
-    // MMAs of tile t-2 read (as P~^T / dS^T): wait until those completed.
+    // Score MMAs.  S^T / dP^T of tile t go to buffer t&1, whose halves the
+    // dV / dK MMAs of tile t-2 read (as P~^T / dS^T): S^T waits only for the
+    // dV MMAs, dP^T for the dK MMAs, so S^T enters the pipe while dK runs.
     if (lane == 0 && nq > 0) {
       bool ok = mbar_wait(&bars->res_full, 0, ctl);
       for (int t = 0; ok && t < nq; ++t) {
         const int s = t % kBwdStages, sb = t & 1;
+        const uint32_t ph = ((t >> 1) - 1) & 1;
         if (!mbar_wait(&bars->st_full[s], (t / kBwdStages) & 1, ctl) ||
-            (t >= 2 && !mbar_wait(&bars->g_done[sb], ((t >> 1) - 1) & 1, ctl))) {
+            (t >= 2 && !mbar_wait(&bars->gv_done[sb], ph, ctl))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        bwd_issue_scores<DQK, DV, Cfg>(tmem, sbase, s, sb);  // S^T = K Q^T, dP^T = V dO^T
+        bwd_issue_scores_half<DQK, Cfg, Cfg::kS, Cfg::kResAOff, Cfg::kStAOff, Cfg::kStA>(tmem, sbase, s, sb);
+        if (t >= 2 && !mbar_wait(&bars->gk_done[sb], ph, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bwd_issue_scores_half<DV, Cfg, Cfg::kDP, Cfg::kResBOff, Cfg::kStBOff, Cfg::kStB>(tmem, sbase, s, sb);
         mma_commit(&bars->s_full[sb]);
       }
       mma_commit(&bars->mma_done);
@@ -350,10 +354,11 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
         // dV += P~^T dO_t ; dK += dS^T Q_t
         bwd_issue_acc<DV>(tmem + Cfg::kAcc0, tmem + Cfg::kS + sb * kBwdTile, sbase + Cfg::kStBOff + s * Cfg::kStB,
                           t == 0);
+        mma_commit(&bars->gv_done[sb]);
         bwd_issue_acc<DQK>(tmem + Cfg::kAcc1, tmem + Cfg::kDP + sb * kBwdTile, sbase + Cfg::kStAOff + s * Cfg::kStA,
                            t == 0);
         mma_commit(&bars->st_empty[s]);
-        mma_commit(&bars->g_done[sb]);
+        mma_commit(&bars->gk_done[sb]);
       }
       mma_commit(&bars->acc_done);
       mma_commit(&bars->mma_done2);
