@@ -278,6 +278,39 @@ __device__ __forceinline__ void dq_elems(const uint32_t* sv, const uint32_t* dpv
   }
 }
 
+// dq_elems with dropout over a thread's two 32-column halves at once (no
+// masking): element c of each half in the same iteration, each half with its
+// own RNG walker, so the two 64-bit carry chains interleave.
+template <bool DROP>
+__device__ __forceinline__ void dq_elems_x2(const uint32_t* sv, const uint32_t* dpv, float sl2, float lse2,
+                                            float delta, float dp_inv, LcgWalk& st0, LcgWalk& st1, uint32_t thr_m1,
+                                            uint32_t* dk) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      LcgWalk& st = h ? st1 : st0;
+      const int cc = 32 * h + c;
+      float pr0 = ex2(fmaf(__uint_as_float(sv[cc]), sl2, -lse2));
+      float pr1 = ex2(fmaf(__uint_as_float(sv[cc + 1]), sl2, -lse2));
+      pr0 = pr0 > kEps ? pr0 : 0.0f;  // skip rule
+      pr1 = pr1 > kEps ? pr1 : 0.0f;
+      float kf0 = 1.0f, kf1 = 1.0f;  // see dkdv_elems: dS = p (kf dP - D)
+      if (DROP) {
+        const bool dr0 = st.dropped(thr_m1);
+        st.step();
+        const bool dr1 = st.dropped(thr_m1);
+        st.step();
+        kf0 = dr0 ? 0.0f : dp_inv;
+        kf1 = dr1 ? 0.0f : dp_inv;
+      }
+      const float d0 = pr0 * fmaf(kf0, __uint_as_float(dpv[cc]), -delta);
+      const float d1 = pr1 * fmaf(kf1, __uint_as_float(dpv[cc + 1]), -delta);
+      dk[cc / 2] = pack_half2(d0, d1);
+    }
+  }
+}
+
 template <int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kBwdTcThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -716,6 +749,15 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
       tc_fence_before();
       mbar_arrive(&bars->sdp_free);  // S/dP may be overwritten by the next tile's MMAs
       uint32_t dk[32];
+      const int64_t jt = static_cast<int64_t>(t) * TN + col0;  // first key of this thread's 64 columns
+      const bool interior = (p.S_kv - jt >= 64) && (!p.causal || iw0 - jt + 1 >= 64);  // warp-uniform
+      if (DROP && interior) {
+        // both 32-column halves in one interleaved loop: two independent RNG
+        // carry chains per thread (measured faster with dropout only)
+        LcgWalk st0(DROP ? lcg_state(rbase, static_cast<uint64_t>(jt)) : 0);
+        LcgWalk st1(DROP ? lcg_state(rbase, static_cast<uint64_t>(jt + 32)) : 0);
+        dq_elems_x2<DROP>(sv, dpv, sl2, lse2, delta, dp_inv, st0, st1, thr_m1, dk);
+      } else
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int64_t j0 = static_cast<int64_t>(t) * TN + col0 + 32 * h2;
