@@ -289,7 +289,7 @@ def run_ours(args, w):
         # public host-buffer API: batch chunks pipelined over copy-in / compute / copy-out streams
         nonlocal outs_h, d2h
         outs_h = fa.pipeline.train_step_host(hq, hk, hv, hdo, w["seed"], offset, scale=kw["scale"],
-                                             dropout=kw["dropout"], causal_mask=kw["causal_mask"], chunks=4,
+                                             dropout=kw["dropout"], causal_mask=kw["causal_mask"], chunks=8,
                                              device=dev, out=outs_h)
         d2h = sum(x.numel() * x.element_size() for x in outs_h)
 

@@ -35,7 +35,7 @@ def _chunk_buffers(dev, dtype, nb, S_q, S_kv, D_qk, D_v):
     return _buffers[key]
 
 
-def train_step_host(q, k, v, d_o, seed, offset, *, scale=1.0, dropout=0.0, causal_mask=False, chunks=4,
+def train_step_host(q, k, v, d_o, seed, offset, *, scale=1.0, dropout=0.0, causal_mask=False, chunks=8,
                     device=None, out=None):
     """(o, stats, dq, dk, dv) on pinned host memory; q, k, v, d_o pinned host [B, S, D] tensors.
 
