@@ -74,6 +74,7 @@ Params make_params(int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D
   p.dp_keep = 1.0f / p.dp_inv;
   p.drop_thr = p.dropout_on ? drop_threshold(dropout) : 0;
   p.rng_base = seed + offset;
+  p.one = 1;
   p.timeout_ns = g_timeout_ns.load();
   return p;
 }

@@ -41,6 +41,7 @@ struct Params {
   uint64_t drop_thr;    // dropped iff hi32(state) < drop_thr
   uint64_t rng_base;    // seed + offset
   uint64_t timeout_ns;
+  uint32_t one;         // 1: an opaque multiplier for lcg_hi_at
 };
 
 // Element offset of row s of folded batch row bh in a [B/H, S, H, D] tensor.

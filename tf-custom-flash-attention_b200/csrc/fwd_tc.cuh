@@ -639,7 +639,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       const float nmu = -mu;
       if (DROP) {
-        LcgWalk st(lcg_state(rbase, static_cast<uint64_t>(kv0)));
+        const uint64_t s0 = lcg_state(rbase, static_cast<uint64_t>(kv0));
+        const uint32_t s0_lo = static_cast<uint32_t>(s0), s0_hi = static_cast<uint32_t>(s0 >> 32);
 #pragma unroll
         for (int c = 0; c < 128; c += 2) {
           float x0, x1;
@@ -647,10 +648,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const float p0 = ex2(x0), p1 = ex2(x1);
           const int q = (c >> 1) & 1;
           fadd2(rs[2 * q], rs[2 * q + 1], p0, p1);
-          const bool d0 = st.dropped(thr_m1);
-          st.step();
-          const bool d1 = st.dropped(thr_m1);
-          st.step();
+          // state of column kv0 + c is s0 + c * A (dropped iff its hi32 < thr)
+          const bool d0 = lcg_hi_at(s0_lo, s0_hi, p.one, static_cast<uint64_t>(c) * kLcgA) <= thr_m1;
+          const bool d1 = lcg_hi_at(s0_lo, s0_hi, p.one, static_cast<uint64_t>(c + 1) * kLcgA) <= thr_m1;
           r[c / 2] = pack_half2(d0 ? 0.0f : p0, d1 ? 0.0f : p1);
         }
       } else {  // bound by MUFU and the tensor pipe, not by issue: scalar forms
