@@ -29,8 +29,7 @@
 namespace sdpa_b200 {
 namespace tc {
 
-constexpr int kBwdThreads = 320;
-constexpr int kBwdTcThreads = 352;  // dK/dV and dQ kernels: + a second MMA-issuing warp
+constexpr int kBwdTcThreads = 352;  // 8 elementwise warps, TMA producer, two MMA-issuing warps
 constexpr int kBwdRows = 128;   // rows owned by a CTA (TMEM lanes)
 constexpr int kBwdTile = 64;    // rows of each streamed tile
 constexpr int kBwdStages = 3;
