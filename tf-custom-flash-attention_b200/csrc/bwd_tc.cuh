@@ -319,11 +319,11 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
   uint8_t* smem = align1024(smem_raw);
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int64_t b = blockIdx.x % p.B;
+  int64_t b, kt;  // low key tiles see the most causal rows: issued first
+  raster(blockIdx.x, p.B, (p.S_kv + kBwdRows - 1) / kBwdRows, b, kt);
   // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
   const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
   constexpr bool heads = HEADS;
-  const int64_t kt = blockIdx.x / p.B;  // low key tiles see the most causal rows: issued first
   const int64_t n0 = kt * kBwdRows;
   const int n_qtiles = static_cast<int>((p.S_q + kBwdTile - 1) / kBwdTile);
   const int tile0 = p.causal ? static_cast<int>(n0 / kBwdTile) : 0;
@@ -533,11 +533,12 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
   Dq2Barriers* bars = reinterpret_cast<Dq2Barriers*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int64_t n_qt = (p.S_q + kBwdRows - 1) / kBwdRows;
-  const int64_t b = blockIdx.x % p.B;
+  int64_t b, tord;
+  raster(blockIdx.x, p.B, n_qt, b, tord);
   // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
   const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
   constexpr bool heads = HEADS;
-  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
+  const int64_t qt = n_qt - 1 - tord;  // longest causal rows first
   const int64_t m0 = qt * kBwdRows;
   const int64_t n_kv_all = (p.S_kv + TN - 1) / TN;
   const int nkv = static_cast<int>(p.causal ? min(n_kv_all, qt + 1) : n_kv_all);

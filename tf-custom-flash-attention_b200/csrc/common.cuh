@@ -44,6 +44,21 @@ struct Params {
   uint32_t one;         // 1: an opaque multiplier for lcg_hi_at
 };
 
+// CTA order of the tensor-core kernels over (batch row b, tile t): groups of
+// kRasterRows batch rows, tile-major within a group, so that the CTAs resident
+// at the same time share batch rows and the operand they all stream (K/V or
+// Q/dO of the row) comes from L2 rather than HBM; tile order 0 is the
+// heaviest causal tile, so each group still issues heavy tiles first.
+constexpr int kRasterRows = 16;
+__device__ __forceinline__ void raster(int64_t idx, int64_t B, int64_t ntiles, int64_t& b, int64_t& t) {
+  const int64_t per = kRasterRows * ntiles;
+  const int64_t g = idx / per;
+  const int64_t rows = B - g * kRasterRows < kRasterRows ? B - g * kRasterRows : kRasterRows;
+  const int64_t w = idx - g * per;
+  t = w / rows;
+  b = g * kRasterRows + (w - t * rows);
+}
+
 // Element offset of row s of folded batch row bh in a [B/H, S, H, D] tensor.
 __host__ __device__ __forceinline__ int64_t row_offset(int64_t H, int64_t bh, int64_t s, int64_t S, int64_t D) {
   if (H == 1) return (bh * S + s) * D;  // contiguous [B, S, D]: no division

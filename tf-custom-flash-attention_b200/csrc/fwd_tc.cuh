@@ -97,11 +97,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int lane = threadIdx.x & 31;
 
   const int64_t n_qt = (p.S_q + kBM - 1) / kBM;
-  const int64_t b = blockIdx.x % p.B;
+  int64_t b, tord;
+  raster(blockIdx.x, p.B, n_qt, b, tord);
   // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
   const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
   constexpr bool heads = HEADS;
-  const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // longest causal rows first
+  const int64_t qt = n_qt - 1 - tord;  // longest causal rows first
   const int64_t m0 = qt * kBM;
   const int64_t n_kv_all = (p.S_kv + kBN - 1) / kBN;
   const int n_kv = static_cast<int>(p.causal ? min(n_kv_all, qt + 1) : n_kv_all);
@@ -433,11 +434,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int lane = threadIdx.x & 31;
 
   const int64_t n_pairs = (p.S_q + 2 * kBM - 1) / (2 * kBM);
-  const int64_t b = blockIdx.x % p.B;
+  int64_t b, tord;
+  raster(blockIdx.x, p.B, n_pairs, b, tord);
   // head and outer batch of folded row b (layout [B/H, S, H, D] when HEADS)
   const int hb = HEADS ? static_cast<int>(b % p.H) : 0, ob = HEADS ? static_cast<int>(b / p.H) : static_cast<int>(b);
   constexpr bool heads = HEADS;
-  const int64_t pq = n_pairs - 1 - blockIdx.x / p.B;  // longest causal rows first
+  const int64_t pq = n_pairs - 1 - tord;  // longest causal rows first
   const int64_t m0 = pq * 2 * kBM;
   const int64_t n_kv_all = (p.S_kv + kBN - 1) / kBN;
   // key tiles per query tile; tile A never needs more than tile B
