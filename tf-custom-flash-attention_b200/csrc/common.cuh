@@ -49,7 +49,10 @@ struct Params {
 // at the same time share batch rows and the operand they all stream (K/V or
 // Q/dO of the row) comes from L2 rather than HBM; tile order 0 is the
 // heaviest causal tile, so each group still issues heavy tiles first.
-constexpr int kRasterRows = 16;
+#ifndef SDPA_B200_RASTER_ROWS
+#define SDPA_B200_RASTER_ROWS 16
+#endif
+constexpr int kRasterRows = SDPA_B200_RASTER_ROWS;
 __device__ __forceinline__ void raster(int64_t idx, int64_t B, int64_t ntiles, int64_t& b, int64_t& t) {
   const int64_t per = kRasterRows * ntiles;
   const int64_t g = idx / per;
