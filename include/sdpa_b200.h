@@ -60,7 +60,9 @@ int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* 
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v);
 
 /* Backward: dq, dk, dv shaped like q, k, v (dtype), from q, k, v, out, stats
- * and d_out of the forward.  Two kernels, dK/dV then dQ, no atomics.
+ * and d_out of the forward, no atomics: fp16 runs two kernels, dQ (which
+ * also writes rowsum(dO*O) to the workspace) then dK/dV; fp32 runs three
+ * (dQ, dK, dV) on the 3xTF32 tensor-core path.
  * Replaces FlashAttnGradFunctor<GPUDevice,T> (sdpa/sdpa_bwd.cu.cc:347-453). */
 int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
                   const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,

@@ -38,6 +38,11 @@ def test_path_selection():
     assert fa.kernel_path(torch.float16, 128, 128) == "tcgen05"
     assert fa.kernel_path(torch.float16, 64, 40) == "tcgen05"
     assert fa.kernel_path(torch.float16, 5, 3) == "simt"
+    assert fa.kernel_path(torch.float32, 64, 128) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 32, 4, backward=True) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 128, 128) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 128, 128, backward=True) == "simt"
+    assert fa.kernel_path(torch.float32, 5, 3) == "simt"
 
 
 def test_argument_errors_without_gpu():

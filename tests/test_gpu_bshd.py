@@ -30,8 +30,11 @@ def unfold(x, B, H):  # [B*H, S, D] -> [B, S, H, D]
     (torch.float16, 2, 4, 256, 256, 128, 128, True, 0.1),    # tcgen05 path
     (torch.float16, 3, 2, 200, 200, 64, 64, True, 0.0),      # ragged rows, causal edge
     (torch.float16, 2, 3, 130, 333, 64, 128, False, 0.2),    # D_qk != D_v, S_q != S_kv
-    (torch.float16, 1, 5, 96, 96, 32, 32, False, 0.1),       # SIMT path (D = 32)
-    (torch.float32, 2, 2, 70, 150, 64, 64, False, 0.05),     # fp32 (SIMT)
+    (torch.float16, 1, 5, 96, 96, 32, 32, False, 0.1),       # tcgen05 path, D = 32 (zero-filled to 64)
+    (torch.float16, 1, 3, 64, 64, 12, 20, False, 0.1),       # SIMT path (rows not 16-byte multiples)
+    (torch.float32, 2, 2, 70, 150, 64, 64, False, 0.05),     # fp32, 3xTF32 tensor-core path
+    (torch.float32, 1, 2, 96, 96, 100, 36, True, 0.1),       # fp32, D_qk > 64: 3xTF32 forward, SIMT backward
+    (torch.float32, 1, 2, 40, 40, 6, 10, False, 0.0),        # fp32 SIMT path
 ])
 def test_bshd_equals_folded_bitwise(dtype, B, H, S_q, S_kv, D_qk, D_v, causal, p):
     g = torch.Generator(device="cuda").manual_seed(B * 100 + H)

@@ -104,6 +104,23 @@ bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, 
   return true;
 }
 
+// fp32 on the 3xTF32 tensor-core kernels: rows must be 16-byte multiples
+// (TMA strides), every pointer 16-byte aligned; the backward serves D_qk <= 64.
+bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
+                 const void* o) {
+  if (force_simt() || dtype != SDPA_B200_F32 || S_kv == 0) return false;
+  if (D_qk % 4 != 0 || D_v % 4 != 0) return false;
+  return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
+}
+
+bool tf32_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n) {
+  if (force_simt() || dtype != SDPA_B200_F32 || S_q == 0 || S_kv == 0) return false;
+  if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return false;
+  for (int i = 0; i < n; ++i)
+    if (!aligned16(ptrs[i])) return false;
+  return true;
+}
+
 // --------------------------------------------------------- diagnostics
 __global__ void dropout_mask_kernel(Params p, uint8_t* mask) {
   const int64_t n = p.B * p.S_q * p.S_kv;
@@ -155,6 +172,7 @@ static int fwd_impl(int dtype, const void* q, const void* k, const void* v, void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int r = bind_context()) return r;
   if (tc_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return launch_fwd_tc(p, st, &t_launches);
+  if (tf32_fwd_ok(dtype, S_kv, D_qk, D_v, q, k, v, out)) return launch_fwd_tf32(p, st, &t_launches);
   return dtype == SDPA_B200_F16 ? launch_fwd_simt_f16(p, st, &t_launches) : launch_fwd_simt_f32(p, st, &t_launches);
 }
 
@@ -211,6 +229,7 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (int r = bind_context()) return r;
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
+  if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tf32(p, st, &t_launches);
   return dtype == SDPA_B200_F16 ? launch_bwd_simt_f16(p, st, &t_launches) : launch_bwd_simt_f32(p, st, &t_launches);
 }
 
@@ -276,7 +295,7 @@ int sdpa_b200_device_status(unsigned int* word, void* stream) {
   const unsigned int zero = 0;
   if (cudaMemcpyFromSymbol(&w, g_status_word, sizeof(w)) != cudaSuccess) return SDPA_B200_ECUDA;
   if (cudaMemcpyToSymbol(g_status_word, &zero, sizeof(zero)) != cudaSuccess) return SDPA_B200_ECUDA;
-  if (status_exchange_fwd_tc(&w) || status_exchange_bwd_tc(&w) || status_exchange_simt_fwd_f16(&w) ||
+  if (status_exchange_fwd_tc(&w) || status_exchange_bwd_tc(&w) || status_exchange_tf32(&w) || status_exchange_simt_fwd_f16(&w) ||
       status_exchange_simt_fwd_f32(&w) || status_exchange_simt_bwd_f16(&w) || status_exchange_simt_bwd_f32(&w)) return SDPA_B200_ECUDA;
   if (word) *word = w;
   return (w & kStatusTimeout) ? SDPA_B200_ETIMEOUT : SDPA_B200_OK;
@@ -290,9 +309,10 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
-  (void)backward;
-  if (force_simt() || dtype != SDPA_B200_F16) return 0;
-  return (D_qk % 8 == 0 && D_v % 8 == 0) ? 1 : 0;
+  if (force_simt()) return 0;
+  if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0) ? 1 : 0;
+  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (!backward || D_qk <= 64)) return 2;
+  return 0;
 }
 
 int sdpa_b200_last_launch_count(void) { return t_launches; }

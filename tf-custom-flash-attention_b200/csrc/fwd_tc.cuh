@@ -51,6 +51,7 @@ struct FwdBarriers {
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_done;
+  uint64_t o_final;  // every PV MMA done (one phase)
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&bars->p_full[s], kBM);
     }
     mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->o_final, 1);
     mbar_init(&bars->mma_done, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -218,6 +220,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
       if (ok) issue_pv(n_kv - 1);
+      mma_commit(&bars->o_final);
       // Every MMA issued so far must finish before TMEM is released.
       mma_commit(&bars->mma_done);
       WaitCtl drain = ctl;
@@ -334,7 +337,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_arrive(&bars->p_full[s]);
     }
     // ----------------------------------------------------------- epilogue
-    if (ok && n_kv > 0) ok = warp_wait(&bars->o_done, (n_kv - 1) & 1, ctl);
+    // Not o_done with parity (n_kv - 1) & 1: PV(j-1) is issued after S(j), so
+    // o_done may still be two phases behind here and that parity would match
+    // an older phase.
+    if (ok && n_kv > 0) ok = warp_wait(&bars->o_final, 0, ctl);
     if (ok) {
       tc_fence_after();
       float lse, inv;

@@ -54,35 +54,48 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// fp16 tensor [B/H, S, H, D] as a 4-D map over (column, head, row, outer
-// batch), box = 64 columns x 1 head x `rows` rows x 1; for H = 1 (contiguous
-// [B, S, D]) the 3-D map (column, row, batch), box 64 x `rows` x 1.  128B
-// swizzle; the shared-memory tile is the same either way.  Columns beyond D
-// and rows beyond S read as zero.  Failures record their detail.
-inline bool make_map_f16(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S, int64_t D, int rows) {
+// Tensor [B/H, S, H, D] of `esize`-byte elements as a 4-D map over (column,
+// head, row, outer batch), box = one 128-byte row segment (64 halves or 32
+// floats) x 1 head x `rows` rows x 1; for H = 1 (contiguous [B, S, D]) the 3-D
+// map (column, row, batch), box 128 B x `rows` x 1.  128B swizzle by default;
+// the shared-memory tile is the same either way.  Columns beyond D and rows
+// beyond S read as zero.  Failures record their detail.
+inline bool make_map(CUtensorMap* m, CUtensorMapDataType dtype, int esize, const void* base, int64_t B, int64_t H,
+                     int64_t S, int64_t D, int rows, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return map_failure(0, "cuTensorMapEncodeTiled unavailable");
   if (H < 1 || B % H != 0) return map_failure(static_cast<int>(H), "bad head count");
+  const cuuint32_t inner = static_cast<cuuint32_t>(128 / esize);
+  const cuuint64_t es = static_cast<cuuint64_t>(esize);
   if (H == 1) {  // contiguous [B, S, D]: the 3-D map (column, row, batch)
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
-    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(rows), 1};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * es, static_cast<cuuint64_t>(S * D) * es};
+    cuuint32_t box[3] = {inner, static_cast<cuuint32_t>(rows), 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = fn(m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
   }
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(B / H)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(H * D * 2),
-                           static_cast<cuuint64_t>(S * H * D * 2)};
-  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D) * es, static_cast<cuuint64_t>(H * D) * es,
+                           static_cast<cuuint64_t>(S * H * D) * es};
+  cuuint32_t box[4] = {inner, 1, static_cast<cuuint32_t>(rows), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dtype, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
+}
+inline bool make_map_f16(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S, int64_t D, int rows) {
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, B, H, S, D, rows);
+}
+inline bool make_map_f32(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S, int64_t D, int rows) {
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, B, H, S, D, rows);
+}
+// fp32 tiles read only as MN-major tf32 operands (32-byte swizzle atoms).
+inline bool make_map_f32_mn(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S, int64_t D, int rows) {
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, B, H, S, D, rows, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 // Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
@@ -114,6 +127,8 @@ inline void record_bwd_event(int i, cudaStream_t st) {
 // Launchers, one per translation unit (launch count added to *launches).
 int launch_fwd_tc(const Params& p, cudaStream_t st, int* launches);
 int launch_bwd_tc(const Params& p, cudaStream_t st, int* launches);
+int launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches);
+int launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches);
 int launch_fwd_simt_f16(const Params& p, cudaStream_t st, int* launches);
 int launch_fwd_simt_f32(const Params& p, cudaStream_t st, int* launches);
 int launch_bwd_simt_f16(const Params& p, cudaStream_t st, int* launches);
@@ -121,6 +136,7 @@ int launch_bwd_simt_f32(const Params& p, cudaStream_t st, int* launches);
 // Reads and clears the status word of each translation unit's kernels.
 int status_exchange_fwd_tc(unsigned int* w);
 int status_exchange_bwd_tc(unsigned int* w);
+int status_exchange_tf32(unsigned int* w);
 int status_exchange_simt_fwd_f16(unsigned int* w);
 int status_exchange_simt_fwd_f32(unsigned int* w);
 int status_exchange_simt_bwd_f16(unsigned int* w);

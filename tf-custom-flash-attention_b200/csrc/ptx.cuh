@@ -147,6 +147,26 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The same products for fp32 data read as tf32 (K = 8 per instruction; the
+// operands hold tf32 values, i.e. fp32 with the 13 low mantissa bits zero).
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive (once) on `bar` when every tcgen05 op issued so far by this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -184,6 +204,13 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])                                         \
       : "memory")
 
+#define SDPA_TMEM_LD16(taddr, r)                                                                                    \
+  asm volatile(                                                                                                    \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"      \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),  \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])                   \
+      : "r"(taddr))
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -205,6 +232,22 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// MN-major operand of 32-bit (tf32) elements: the only layout the tensor
+// cores take for it is the 128-byte swizzle with 32-byte atoms (descriptor
+// layout type 1): rows of 128 B (32 elements along M/N), the 32-byte chunk
+// index XORed with (row & 3); sbo = byte distance between 4-row K groups,
+// lbo = byte distance to the next 32-wide M/N block.  TMA writes it with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+__device__ __forceinline__ uint64_t make_sw128_32b_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(1) << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // Instruction descriptor for kind::f16 (fp16 x fp16 -> fp32) or kind::tf32.
 //   a_mn / b_mn: 1 when the operand is M/N-major in shared memory.
 __host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool a_mn, bool b_mn, bool tf32) {
@@ -214,6 +257,27 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool a_mn, bool 
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17)      // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
+}
+
+// ------------------------------------------------------------- 3xTF32
+// x = hi + lo with hi, lo both tf32 values: hi = x rounded to tf32 (nearest,
+// ties away), lo = the rounded remainder.  A product a*b is then taken as
+// ah*bh + ah*bl + al*bh, whose error is about 2^-21 of |a*b| (al*bl and the
+// rounding of the remainders are what is dropped), against 2^-11 for one
+// tf32 product.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - hi);
+}
+// Generic-proxy writes to shared memory become visible to the async proxy
+// (TMA, tcgen05.mma operand reads) after this fence.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // -------------------------------------------------------------- math bits

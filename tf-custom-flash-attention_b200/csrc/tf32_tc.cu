@@ -1,0 +1,98 @@
+// Translation unit: fp32 (3xTF32) tcgen05 forward and backward kernels
+#include "host.cuh"
+#include "ptx.cuh"
+#include "tf32_bwd.cuh"
+#include "tf32_fwd.cuh"
+
+using namespace sdpa_b200;
+using namespace sdpa_b200::host;
+
+namespace {
+
+template <int DQK, int DV, bool DROP, bool HEADS>
+int launch_fwd_t(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tf32::FwdCfg<DQK, DV>;
+  auto kern = tf32::fwd_kernel<DQK, DV, DROP, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
+  CUtensorMap mk, mv;
+  if (!make_map_f32(&mk, p.k, p.B, p.H, p.S_kv, p.D_qk, Cfg::kBN) ||
+      !make_map_f32_mn(&mv, p.v, p.B, p.H, p.S_kv, p.D_v, Cfg::kBN))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map
+  const int64_t grid = ((p.S_q + tf32::kBM - 1) / tf32::kBM) * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tf32::kFwdThreads, Cfg::kSmemBytes, st>>>(mk, mv, p);
+  ++*launches;
+  return launch_result();
+}
+
+template <int DQK, int DV>
+int launch_fwd_d(const Params& p, cudaStream_t st, int* launches) {
+  if (p.H > 1)
+    return p.dropout_on ? launch_fwd_t<DQK, DV, true, true>(p, st, launches)
+                        : launch_fwd_t<DQK, DV, false, true>(p, st, launches);
+  return p.dropout_on ? launch_fwd_t<DQK, DV, true, false>(p, st, launches)
+                      : launch_fwd_t<DQK, DV, false, false>(p, st, launches);
+}
+
+template <int MODE, int DQK, int DV, bool DROP, bool HEADS>
+int launch_bwd_mode(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tf32::BwdCfg<MODE, DQK, DV>;
+  auto kern = tf32::bwd_kernel<MODE, DQK, DV, DROP, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
+  const bool rows_q = MODE == tf32::kDQ;
+  CUtensorMap ma, mb;
+  // streamed tiles: K, V (DQ) or Q, dO (DK, DV); DV reads dO only MN-major
+  const int64_t S_str = rows_q ? p.S_kv : p.S_q;
+  const bool ok_a = make_map_f32(&ma, rows_q ? p.k : p.q, p.B, p.H, S_str, p.D_qk, Cfg::kN);
+  const bool ok_b = MODE == tf32::kDV ? make_map_f32_mn(&mb, p.d_o, p.B, p.H, S_str, p.D_v, Cfg::kN)
+                                      : make_map_f32(&mb, rows_q ? p.v : p.d_o, p.B, p.H, S_str, p.D_v, Cfg::kN);
+  if (!ok_a || !ok_b) return SDPA_B200_ECUDA;  // detail recorded by make_map
+  const int64_t grid = (((rows_q ? p.S_q : p.S_kv) + 127) / 128) * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tf32::kBwdThreads, Cfg::kSmemBytes, st>>>(ma, mb, p);
+  ++*launches;
+  return launch_result();
+}
+
+// DQ first: it writes D = rowsum(dO * O) (into the workspace), which DK reads.
+template <int DQK, int DV, bool DROP, bool HEADS>
+int launch_bwd_t(const Params& p, cudaStream_t st, int* launches) {
+  sdpa_b200::record_bwd_event(0, st);
+  if (int r = launch_bwd_mode<tf32::kDQ, DQK, DV, DROP, HEADS>(p, st, launches)) return r;
+  sdpa_b200::record_bwd_event(1, st);
+  if (int r = launch_bwd_mode<tf32::kDK, DQK, DV, DROP, HEADS>(p, st, launches)) return r;
+  sdpa_b200::record_bwd_event(2, st);
+  if (int r = launch_bwd_mode<tf32::kDV, DQK, DV, DROP, HEADS>(p, st, launches)) return r;
+  sdpa_b200::record_bwd_event(3, st);
+  return SDPA_B200_OK;
+}
+
+template <int DQK, int DV>
+int launch_bwd_d(const Params& p, cudaStream_t st, int* launches) {
+  if (p.H > 1)
+    return p.dropout_on ? launch_bwd_t<DQK, DV, true, true>(p, st, launches)
+                        : launch_bwd_t<DQK, DV, false, true>(p, st, launches);
+  return p.dropout_on ? launch_bwd_t<DQK, DV, true, false>(p, st, launches)
+                      : launch_bwd_t<DQK, DV, false, false>(p, st, launches);
+}
+
+}  // namespace
+
+int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) {
+  const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
+  if (q128 && v128) return launch_fwd_d<128, 128>(p, st, launches);
+  if (q128) return launch_fwd_d<128, 64>(p, st, launches);
+  if (v128) return launch_fwd_d<64, 128>(p, st, launches);
+  return launch_fwd_d<64, 64>(p, st, launches);
+}
+
+// D_qk <= 64 only (the caller checks): with D_qk = 128 the resident operands
+// and accumulators of the DQ pass exceed TMEM.
+int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
+  if (p.D_v > 64) return launch_bwd_d<64, 128>(p, st, launches);
+  return launch_bwd_d<64, 64>(p, st, launches);
+}
+
+SDPA_B200_STATUS_EXCHANGE(tf32)

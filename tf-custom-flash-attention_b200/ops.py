@@ -267,8 +267,9 @@ def device_status(device=None) -> int:
 
 
 def kernel_path(dtype: torch.dtype, D_qk: int, D_v: int, backward: bool = False) -> str:
-    """'tcgen05' or 'simt': which kernel family serves this shape."""
-    return "tcgen05" if _lib.lib().sdpa_b200_path(_DTYPES[dtype], D_qk, D_v, int(backward)) else "simt"
+    """'tcgen05' (fp16), 'tcgen05-3xtf32' (fp32) or 'simt': which kernel family serves this shape."""
+    return {1: "tcgen05", 2: "tcgen05-3xtf32"}.get(_lib.lib().sdpa_b200_path(_DTYPES[dtype], D_qk, D_v, int(backward)),
+                                                   "simt")
 
 
 def last_launch_count() -> int:
