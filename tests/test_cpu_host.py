@@ -40,7 +40,8 @@ def test_path_selection():
     assert fa.kernel_path(torch.float16, 5, 3) == "simt"
     assert fa.kernel_path(torch.float32, 64, 128) == "tcgen05-3xtf32"
     assert fa.kernel_path(torch.float32, 32, 4, backward=True) == "tcgen05-3xtf32"
-    assert fa.kernel_path(torch.float32, 128, 128) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 128, 64) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 128, 128) == "simt"
     assert fa.kernel_path(torch.float32, 128, 128, backward=True) == "simt"
     assert fa.kernel_path(torch.float32, 5, 3) == "simt"
 

@@ -110,6 +110,9 @@ bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void*
                  const void* o) {
   if (force_simt() || dtype != SDPA_B200_F32 || S_kv == 0) return false;
   if (D_qk % 4 != 0 || D_v % 4 != 0) return false;
+  // With both over 64 the output has no TMEM room for a round-to-nearest
+  // running total and its error grows with S_kv past 1e-5: SIMT serves it.
+  if (D_qk > 64 && D_v > 64) return false;
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
 }
 
@@ -311,7 +314,8 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
   if (force_simt()) return 0;
   if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0) ? 1 : 0;
-  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (!backward || D_qk <= 64)) return 2;
+  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (backward ? D_qk <= 64 : (D_qk <= 64 || D_v <= 64)))
+    return 2;
   return 0;
 }
 

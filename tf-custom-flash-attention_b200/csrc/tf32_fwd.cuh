@@ -48,7 +48,8 @@ struct FwdCfg {
   // room, PV accumulates only kFlush tiles at a time (fresh accumulator at
   // every kFlush-th tile) and the softmax threads add each segment into a
   // running total OT (separate TMEM columns) in fp32 round-to-nearest.  With
-  // D_qk and D_v both over 64 there is no room and O accumulates in the MMA.
+  // D_qk and D_v both over 64 there is no room (kFlush = 0); the library
+  // sends those shapes to the SIMT kernels.
   static constexpr bool kFits64 = 2 * DQK + 2 * DV + 4 * 64 <= 512;
   static constexpr bool kFits32 = 2 * DQK + 2 * DV + 4 * 32 <= 512;
   static constexpr int kBN = kFits64 ? 64 : 32;
