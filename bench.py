@@ -6,9 +6,16 @@ Workload (default, BASELINE.json configs[3], the long-context training case
 the north-star targets are quoted on): fp16 q/k/v [32, 8192, 128] ~N(0,1),
 causal, dropout 0.1, seed 7, offset 0, scale 1/sqrt(128); one step = forward
 (Sdpa) + backward (SdpaGrad) with d_o ~N(0,1).  Synthetic seeded inputs.
-Multi-GPU: weak scaling, every rank owns its own 32 batch rows (global rows
-rank*32 ..), dropout offset rebased so masks equal an unsharded run; no
-collective on the data path; time = max over ranks.
+Multi-GPU (--gpus N under torchrun): strong scaling.  The workload's global
+batch is split into contiguous shards (sharding.shard_rows; cfg4: 32/16/8/4
+rows per GPU at N = 1/2/4/8), each rank's dropout offset rebased
+(sharding.shard_offset) so masks equal the unsharded run; no collective on the
+data path; time = max over ranks.  Outside the timed region the first row of
+every shard (o, stats, dq, dk, dv) is all-gathered over NCCL to rank 0, which
+recomputes those global rows alone and checks them bit for bit ("validated").
+The weak-scaling figure (every rank the full per-GPU batch) is reported beside
+it, as are each rank's pinned host<->device copy bandwidths measured alone and
+with all ranks copying at once (what bounds the end-to-end number).
 
 FLOPs per step (algorithmic, causal halves both): fwd 2*S^2*(Dqk+Dv)*B/2,
 bwd 2*S^2*(3*Dqk+2*Dv)*B/2.
@@ -180,19 +187,72 @@ def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        pass
+    warm = min(args.warmup, 1)  # each step is seconds of CPU work: one real warm-up step
+    if warm:
+        time_reference_cpu(w, steps=1)
     val, threads, sample, t = time_reference_cpu(w, steps=max(1, args.steps))
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+        "steps": args.steps, "warmup": warm, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
         "config": {"workload": args.workload, **{k: w[k] for k in ("B", "S", "D_qk", "D_v", "causal", "dropout")},
                    "S_kv": seqs(w)[1]},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def make_rows(w, b0, b1, dev, dt):
+    """Inputs q, k, v, d_o of global batch rows [b0, b1): each row from its own seeded
+    generator, so any rank can rebuild any row."""
+    import torch
+
+    Dq, Dv = w["D_qk"], w["D_v"]
+    S, S_kv = seqs(w)
+    std = w.get("std", 1.0)
+    out = [torch.empty((b1 - b0, n, d), dtype=dt, device=dev) for n, d in ((S, Dq), (S_kv, Dq), (S_kv, Dv), (S, Dv))]
+    g = torch.Generator(device=dev)
+    for b in range(b0, b1):
+        g.manual_seed(1000003 * (b + 1))
+        for t in out:
+            t[b - b0].copy_(torch.randn(t.shape[1:], generator=g, device=dev, dtype=torch.float32) * std)
+    out[3].div_(std)  # d_o ~ N(0, 1)
+    return out
+
+
+def host_copy_bandwidth(dev, world, rank, nbytes=1 << 28):
+    """Pinned host <-> device copy GB/s of this rank: alone (ranks take turns) and
+    with every rank copying at once."""
+    import torch
+
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    def timed(src, dst):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dst.copy_(src, non_blocking=True)  # warm
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        return 3 * nbytes / (a.elapsed_time(b) * 1e-3) / 1e9
+
+    res = {}
+    for name, src, dst in (("h2d", h, d), ("d2h", d, h)):
+        alone = None
+        for r in range(world):
+            if world > 1:
+                torch.distributed.barrier()
+            if r == rank:
+                alone = timed(src, dst)
+        if world > 1:
+            torch.distributed.barrier()
+        res[f"{name}_alone_gbs"] = alone
+        res[f"{name}_concurrent_gbs"] = timed(src, dst)
+    return res
 
 
 def run_ours(args, w):
@@ -202,86 +262,134 @@ def run_ours(args, w):
     torch.cuda.set_device(local)
     fa = importlib.import_module("tf-custom-flash-attention_b200")
     dev = torch.device("cuda", local)
-    B, Dq, Dv = w["B"], w["D_qk"], w["D_v"]
+    B_glob, Dq, Dv = w["B"], w["D_qk"], w["D_v"]
     S, S_kv = seqs(w)
     dt = torch.float16 if w["dtype"] == "f16" else torch.float32
-    b0 = rank * B  # weak scaling: this rank's global batch rows
+    b0, b1 = fa.sharding.shard_rows(B_glob, world, rank)  # strong scaling: this rank's global rows
+    B = b1 - b0
     offset = fa.sharding.shard_offset(w["offset"], b0, S, S_kv)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    std = w.get("std", 1.0)
-    q, k, v, do = ((torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(dt)
-                   for shape in ((B, S, Dq), (B, S_kv, Dq), (B, S_kv, Dv), (B, S, Dv)))
+    q, k, v, do = make_rows(w, b0, b1, dev, dt)
     kw = dict(scale=Dq ** -0.5, dropout=w["dropout"], causal_mask=w["causal"])
     stream = torch.cuda.current_stream()
-
+    path = fa.kernel_path(dt, Dq, Dv, backward=True)
+    # per-kernel timing of the backward on the launching stream, through the
+    # library's diagnostic event hook: fp16 runs dQ then dK/dV, fp32 dQ, dK, dV
+    knames = {"tcgen05": ("dq2_kernel", "dkdv_kernel"), "tcgen05-3xtf32": ("tf32 dQ", "tf32 dK", "tf32 dV")}.get(path)
     launches = [0]
-    # per-kernel timing of the backward (rowsum | dK/dV | dQ) on the launching
-    # stream, through the library's diagnostic event hook (tensor-core path only)
-    per_kernel = fa.kernel_path(dt, Dq, Dv, backward=True) == "tcgen05"
     kev = []
+    last = {}
 
-    def step():
-        o, s = fa.sdpa(q, k, v, w["seed"], offset, **kw)
+    def step(q, k, v, do, off, record=True):
+        o, s = fa.sdpa(q, k, v, w["seed"], off, **kw)
         n = fa.last_launch_count()
         e_mid = torch.cuda.Event(enable_timing=True)
         e_mid.record(stream)
-        if per_kernel:
+        if knames and record:
             evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             for e in evs:  # torch creates the CUDA event on its first record
                 e.record(stream)
             arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
             fa._lib.lib().sdpa_b200_set_bwd_events(arr, 4)
             kev.append(evs)
-        dq, dk, dv = fa.sdpa_grad(q, k, v, o, s, do, w["seed"], offset, **kw)
-        if per_kernel:
+        dq, dk, dv = fa.sdpa_grad(q, k, v, o, s, do, w["seed"], off, **kw)
+        if knames and record:
             fa._lib.lib().sdpa_b200_set_bwd_events(None, 0)
         launches[0] += n + fa.last_launch_count()
+        last.update(o=o, s=s, dq=dq, dk=dk, dv=dv)
         return e_mid
 
+    def timed_loop(q, k, v, do, off, steps, record=True):
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        evs = []
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        prev = e0
+        for _ in range(steps):
+            mid = step(q, k, v, do, off, record)
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(stream)
+            evs.append((prev, mid, end))
+            prev = end
+        torch.cuda.synchronize()
+        return e0.elapsed_time(prev), evs
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
     for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
+        step(q, k, v, do, offset, record=False)
     clocks = ClockSampler(local)
     clocks.start()
     launches[0] = 0
     kev.clear()
-    evs = []
-    e0 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    prev = e0
-    for _ in range(args.steps):
-        mid = step()
-        end = torch.cuda.Event(enable_timing=True)
-        end.record(stream)
-        evs.append((prev, mid, end))
-        prev = end
-    torch.cuda.synchronize()
-    total_ms = e0.elapsed_time(prev)
+    total_ms, evs = timed_loop(q, k, v, do, offset, args.steps)
+    timed_launches = launches[0]
+    clk = clocks.stop()
     fwd_ms = sum(a.elapsed_time(m) for a, m, _ in evs) / args.steps
     bwd_ms = sum(m.elapsed_time(e) for _, m, e in evs) / args.steps
     kernel_ms = None
-    if per_kernel and len(kev) == args.steps:
-        kernel_ms = {name: sum(e[i].elapsed_time(e[i + 1]) for e in kev) / args.steps
-                     for i, name in enumerate(("dq", "dkdv"))}
-    clk = clocks.stop()
-    per_rank = [{"rank": rank, "ms_per_step": total_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
+    if knames and len(kev) == args.steps:
+        kernel_ms = {name: sum(e[i].elapsed_time(e[i + 1]) for e in kev) / args.steps for i, name in enumerate(knames)}
+    my_ms = total_ms / args.steps
+    total_ms = max_over_ranks(total_ms)
+    per_rank = [{"rank": rank, "rows": [b0, b1], "ms_per_step": my_ms, "sm_mhz": clk.get("sm_mhz"),
                  "reasons": clk.get("reasons")}]
+
+    # ---- validation over NCCL (outside the timed region): the first row of every
+    # shard, recomputed alone on rank 0 with the global offset, must match bit for bit
+    names = ("o", "s", "dq", "dk", "dv")
+    sample = [last[n][0].contiguous() for n in names]
     if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = float(t.item())
-        gathered = [None] * world
-        torch.distributed.all_gather_object(gathered, per_rank[0])
-        per_rank = gathered
-        torch.distributed.barrier()
+        gathered = []
+        for t in sample:
+            bufs = [torch.empty_like(t) for _ in range(world)]
+            torch.distributed.all_gather(bufs, t)
+            gathered.append(bufs)
+        starts = [fa.sharding.shard_rows(B_glob, world, r)[0] for r in range(world)]
+    else:
+        gathered = [[t] for t in sample]
+        starts = [b0]
+    validated, mismatched = None, []
+    if rank == 0:
+        validated = True
+        for r, gb in enumerate(starts):
+            rq, rk, rv, rdo = make_rows(w, gb, gb + 1, dev, dt)
+            off_r = fa.sharding.shard_offset(w["offset"], gb, S, S_kv)
+            step(rq, rk, rv, rdo, off_r, record=False)
+            for n, bufs in zip(names, gathered):
+                if not torch.equal(last[n][0], bufs[r]):
+                    validated = False
+                    mismatched.append([gb, n])
+        torch.cuda.synchronize()
+
+    # ---- weak scaling beside it (every rank the full per-GPU batch), N > 1 only
+    weak = None
+    if world > 1:
+        wq, wk, wv, wdo = make_rows(w, rank * B_glob, (rank + 1) * B_glob, dev, dt)
+        woff = fa.sharding.shard_offset(w["offset"], rank * B_glob, S, S_kv)
+        step(wq, wk, wv, wdo, woff, record=False)
+        wsteps = max(1, min(args.steps, 5))
+        wms, _ = timed_loop(wq, wk, wv, wdo, woff, wsteps, record=False)
+        wms = max_over_ranks(wms) / wsteps
+        ff, fb = flops(w)
+        weak = {"per_gpu_batch": B_glob, "global_batch": B_glob * world, "ms_per_step": wms,
+                "value": world * (ff + fb) / (wms * 1e-3) / 1e12, "unit": "TFLOP/s"}
+        del wq, wk, wv, wdo
+
+    # ---- host copy bandwidth (what bounds the end-to-end number)
+    copy_bw = host_copy_bandwidth(dev, world, rank)
+    per_rank[0].update({k2: round(v2, 2) for k2, v2 in copy_bw.items()})
 
     # ---- end to end through the public API: pinned host inputs in, results out, every step
     hq, hk, hv, hdo = (x.cpu().pin_memory() for x in (q, k, v, do))
     outs_h = None
-    e2e_ms = None
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
     d2h = 0
 
@@ -289,8 +397,8 @@ def run_ours(args, w):
         # public host-buffer API: batch chunks pipelined over copy-in / compute / copy-out streams
         nonlocal outs_h, d2h
         outs_h = fa.pipeline.train_step_host(hq, hk, hv, hdo, w["seed"], offset, scale=kw["scale"],
-                                             dropout=kw["dropout"], causal_mask=kw["causal_mask"], chunks=8,
-                                             device=dev, out=outs_h)
+                                             dropout=kw["dropout"], causal_mask=kw["causal_mask"],
+                                             chunks=min(8, B), device=dev, out=outs_h)
         d2h = sum(x.numel() * x.element_size() for x in outs_h)
 
     e2e_steps = max(1, min(args.steps, 5))
@@ -306,28 +414,40 @@ def run_ours(args, w):
         e2e_step()
     b_.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b_) / e2e_steps
+    e2e_ms = max_over_ranks(a.elapsed_time(b_) / e2e_steps)
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        gathered_pr = [None] * world
+        torch.distributed.all_gather_object(gathered_pr, per_rank[0])
+        per_rank = gathered_pr
+        torch.distributed.barrier()
 
-    f_fwd, f_bwd = flops(w)
+    f_fwd, f_bwd = flops(w)  # the whole (global) workload: strong scaling
     ms = total_ms / args.steps
-    value = world * (f_fwd + f_bwd) / (ms * 1e-3) / 1e12
+    value = (f_fwd + f_bwd) / (ms * 1e-3) / 1e12
     peak, peak_kind = peaks()
-    fwd_tf = f_fwd / (fwd_ms * 1e-3) / 1e12
-    bwd_tf = f_bwd / (bwd_ms * 1e-3) / 1e12
-    # Dominant kernel.  Algorithmic FLOPs per launch: fwd = the forward; of the
-    # backward's 5 MMA-units (S, dP, dV, dK, dQ), dK/dV carries 4 and dQ 1 (its
-    # S and dP are recomputation, not algorithmic work).
-    cands = [("fwd_pair_kernel", fwd_ms, f_fwd)]
-    if kernel_ms:
-        cands += [("dkdv_kernel", kernel_ms["dkdv"], 0.8 * f_bwd), ("dq2_kernel", kernel_ms["dq"], 0.2 * f_bwd)]
+    if dt == torch.float32:  # 3xTF32: tf32 runs at half the fp16 rate, three MMAs per product
+        peak, peak_kind = peak / 6.0, f"{peak_kind} bf16 / 6 (3xTF32)"
+    mf_fwd, mf_bwd = flops(w, B=B)  # this rank's share
+    fwd_tf = mf_fwd / (fwd_ms * 1e-3) / 1e12
+    bwd_tf = mf_bwd / (bwd_ms * 1e-3) / 1e12
+    # Dominant kernel and its algorithmic FLOPs per launch.  Of the backward's five
+    # products (S, dP, dV, dK, dQ; 2*S_q*S_kv*D each, D = D_qk for S, dK, dQ and D_v
+    # for dP, dV) fp16's dK/dV kernel carries S, dP, dV, dK and its dQ kernel dQ (its
+    # S and dP are recomputation); fp32's dQ pass carries dQ, dK pass S, dP, dK, dV pass dV.
+    fwd_name = {"tcgen05": "fwd_pair_kernel", "tcgen05-3xtf32": "tf32 forward"}.get(
+        fa.kernel_path(dt, Dq, Dv), "simt forward")
+    unit = mf_bwd / (3 * Dq + 2 * Dv)
+    cands = [(fwd_name, fwd_ms, mf_fwd)]
+    if kernel_ms and path == "tcgen05":
+        cands += [("dkdv_kernel", kernel_ms["dkdv_kernel"], unit * (2 * Dq + 2 * Dv)),
+                  ("dq2_kernel", kernel_ms["dq2_kernel"], unit * Dq)]
+    elif kernel_ms:
+        cands += [("tf32 dQ", kernel_ms["tf32 dQ"], unit * Dq), ("tf32 dK", kernel_ms["tf32 dK"], unit * (2 * Dq + Dv)),
+                  ("tf32 dV", kernel_ms["tf32 dV"], unit * Dv)]
     else:
-        cands += [("bwd (all kernels)", bwd_ms, f_bwd)]
+        cands += [("bwd (all kernels)", bwd_ms, mf_bwd)]
     name, kms, kfl = max(cands, key=lambda c: c[1])
-    dominant = (name, kfl / (kms * 1e-3) / 1e12, kms, kfl)
+    achieved = kfl / (kms * 1e-3) / 1e12
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as fh:
@@ -341,33 +461,41 @@ def run_ours(args, w):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         try:
-            val, threads, sample, _ = time_reference_cpu(w)
-            cpu = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample}
+            val, threads, sample_txt, _ = time_reference_cpu(w)
+            cpu = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample_txt}
         except Exception as e:  # the reference build is missing on this box
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    in_bytes = sum(x.numel() * x.element_size() for x in (q, k, v, do))
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16" if dt == torch.float16 else "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": args.workload, "global_batch": B * world, "per_gpu_batch": B, "seq_len": S,
-                   "seq_len_kv": S_kv,
-                   "D_qk": Dq, "D_v": Dv, "causal": w["causal"], "dropout": w["dropout"],
-                   "parallelism": f"batch-sharded x{world}, no collective",
-                   "l2": (f"inputs {sum(x.numel() * x.element_size() for x in (q, k, v, do)) / 1e6:.0f} MB per step "
-                          + ("(larger than L2)" if sum(x.numel() * x.element_size() for x in (q, k, v, do)) > 126e6
-                             else "(fit in L2: small config)"))},
+        "config": {"workload": args.workload, "global_batch": B_glob, "per_gpu_batch": B, "seq_len": S,
+                   "seq_len_kv": S_kv, "D_qk": Dq, "D_v": Dv, "causal": w["causal"], "dropout": w["dropout"],
+                   "parallelism": f"batch-sharded x{world} (strong scaling), no collective on the data path",
+                   "l2": f"inputs {in_bytes / 1e6:.0f} MB per rank per step "
+                         + ("(larger than L2)" if in_bytes > 126e6 else "(fit in L2: small config)")},
+        "kernel_path": path,
         "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf, "pct_of_peak": 100.0 * value / world / peak,
-        "roofline": {"bound": "tensor", "kernel": dominant[0], "achieved": dominant[1], "peak": peak,
-                     "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": dominant[1] / peak, "traffic": traffic,
-                     "ms_per_launch": dominant[2], "flops_per_launch": dominant[3],
-                     "kernel_ms": kernel_ms, "traffic_source": "profiles/traffic_cfg4.md (ncu, scaled)"},
-        "e2e": {"value": world * (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": launches[0],
+        "roofline": {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic, "ms_per_launch": kms,
+                     "flops_per_launch": kfl, "kernel_ms": kernel_ms},
+        "e2e": {"value": (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "bound": "pinned host<->device copies (see per_rank copy GB/s)"},
+        "validated": validated, "validation": {"rows_checked": starts, "mismatches": mismatched,
+                                               "method": "NCCL all_gather of each shard's first row; rank 0 "
+                                                         "recomputes it alone with the global offset; bit-exact"},
+        "weak_scaling": weak,
+        "gpu_launches": timed_launches,
         "per_rank": per_rank,
         "clocks": clk,
         "cpu_baseline": cpu,
     }
+    if world > 1:
+        line["limiter"] = (f"{B} batch rows per GPU: forward {B * ((S + 255) // 256)} CTAs, backward "
+                           f"{B * ((S + 127) // 128)} CTAs per kernel on 148 SMs"
+                           + (", causal tiles of unequal length" if w["causal"] else ""))
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
