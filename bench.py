@@ -50,6 +50,8 @@ WORKLOADS = {
     "cfg5": dict(B=128, S=512, S_kv=4096, D_qk=64, D_v=128, causal=False, dropout=0.05, seed=0, offset=0,
                  dtype="f32", std=0.5),
 }
+# cuBLAS tf32 matmul, 8192^3, measured on this pool's B200s (profiles/tf32_matmul_peak.md)
+TF32_MATMUL_TFLOPS = 738.7
 METRIC = "fwd and fwd+bwd attention TFLOP/s per B200, % of dense fp16 tensor peak"
 
 
@@ -425,8 +427,8 @@ def run_ours(args, w):
     ms = total_ms / args.steps
     value = (f_fwd + f_bwd) / (ms * 1e-3) / 1e12
     peak, peak_kind = peaks()
-    if dt == torch.float32:  # 3xTF32: tf32 runs at half the fp16 rate, three MMAs per product
-        peak, peak_kind = peak / 6.0, f"{peak_kind} bf16 / 6 (3xTF32)"
+    if dt == torch.float32:  # 3xTF32: three tf32 MMAs per product, tf32 matmul measured on this pool
+        peak, peak_kind = TF32_MATMUL_TFLOPS / 3.0, "measured tf32 matmul / 3 (profiles/tf32_matmul_peak.md)"
     mf_fwd, mf_bwd = flops(w, B=B)  # this rank's share
     fwd_tf = mf_fwd / (fwd_ms * 1e-3) / 1e12
     bwd_tf = mf_bwd / (bwd_ms * 1e-3) / 1e12

@@ -36,6 +36,18 @@ namespace sdpa_b200 {
 namespace tf32 {
 
 enum BwdMode { kDQ = 0, kDK = 1, kDV = 2 };
+
+// Timing probe for tuning builds (-DSDPA_B200_TF32_PROBE): SM cycles spent by
+// the roles of CTA 0 in each phase, summed into slots of g_tf32_probe.
+#ifdef SDPA_B200_TF32_PROBE
+__device__ unsigned long long g_tf32_probe[16];
+#define TF32_PROBE_T0(v) const long long v = clock64()
+#define TF32_PROBE_ADD(slot, t0) \
+  if (blockIdx.x == 0 && MODE == SDPA_B200_TF32_PROBE) atomicAdd(&g_tf32_probe[slot], static_cast<unsigned long long>(clock64() - (t0)))
+#else
+#define TF32_PROBE_T0(v)
+#define TF32_PROBE_ADD(slot, t0)
+#endif
 constexpr int kBwdThreads = 448;
 
 template <int MODE, int DQK, int DV>
@@ -222,7 +234,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int issued = 0;
       for (int t = 0; t < n; ++t) {
         const int s = t % kStages;
+        TF32_PROBE_T0(p0);
         if (!mbar_wait(&bars->st_empty[s], ((t / kStages) & 1) ^ 1, ctl)) break;
+        TF32_PROBE_ADD(8, p0);
         const int row0 = (tile0 + t) * kN;
         mbar_expect_tx(&bars->st_full[s], Cfg::kSABytes + Cfg::kSBBytes);
 #pragma unroll
@@ -253,10 +267,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int t = 0; ok && t <= n; ++t) {
           if (t > 0) {  // dQ / dK (+)= dS(t-1) SA(t-1)
             const int sp = (t - 1) % kStages;
+            TF32_PROBE_T0(w0);
             if (!mbar_wait(&bars->p_full[0], (t - 1) & 1, ctl)) {
               ok = false;
               break;
             }
+            TF32_PROBE_ADD(0, w0);
             tc_fence_after();
             // a fresh accumulator every tile: the elementwise threads fold the
             // previous tile's into their fp32 running total (see below)
@@ -265,14 +281,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           if (t == n) break;
           const int s = t % kStages;
+          TF32_PROBE_T0(w1);
           if (!mbar_wait(&bars->st_ready[s], (t / kStages) & 1, ctl)) {
             ok = false;
             break;
           }
+          TF32_PROBE_ADD(1, w1);
           tc_fence_after();
+          TF32_PROBE_T0(w3);
           issue_scores<DQK, kN>(tT, tmem + Cfg::kXh, tmem + Cfg::kXl, sb + Cfg::sa_hi(s), sb + Cfg::sa_lo(s));
           issue_scores<DV, kN>(tT + kN, tmem + Cfg::kYh, tmem + Cfg::kYl, sb + Cfg::sb_hi(s), sb + Cfg::sb_lo(s));
           mma_commit(&bars->s_full[0]);
+          TF32_PROBE_ADD(3, w3);
         }
       } else {
         // two tile buffers (S^T / P~^T hi, P~^T lo) of 2 kN columns
@@ -315,7 +335,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int tid = threadIdx.x - 256;
     for (int t = 0; t < n; ++t) {
       const int s = t % kStages;
+      TF32_PROBE_T0(c0);
       if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
+      if (tid == 0) TF32_PROBE_ADD(6, c0);
+      TF32_PROBE_T0(c1);
       if (!kRowsAreQueries) {  // lse (log2 units) and D of the tile's query rows
         float* vec = reinterpret_cast<float*>(smem + Cfg::vec(s));
         const int64_t i = static_cast<int64_t>(tile0 + t) * kN + (tid % kN);
@@ -330,6 +353,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         split_tile(smem + Cfg::sa_hi(s), smem + Cfg::sa_lo(s), Cfg::kSABytes, tid, 128);
       split_tile(smem + Cfg::sb_hi(s), smem + Cfg::sb_lo(s), Cfg::kSBBytes, tid, 128);
       fence_proxy_async_smem();
+      if (tid == 0) TF32_PROBE_ADD(7, c1);
       mbar_arrive(&bars->st_ready[s]);
     }
   } else {
@@ -399,11 +423,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int s = t % kStages;
       const int bb = Cfg::kHasY ? 0 : (t & 1);
       const uint32_t ph = Cfg::kHasY ? (t & 1) : ((t >> 1) & 1);
+      TF32_PROBE_T0(e0);
       if (!tc::warp_wait(&bars->s_full[bb], ph, ctl) ||
           (!kRowsAreQueries && !tc::warp_wait(&bars->st_ready[s], (t / kStages) & 1, ctl))) {
         ok = false;
         break;
       }
+      if (threadIdx.x == 0) TF32_PROBE_ADD(4, e0);
+      TF32_PROBE_T0(e1);
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + Cfg::kT + bb * 2 * kN + col0;  // S / S^T (hi written back here)
       const uint32_t tD = tS + kN;                                          // dP / dP^T, or P~^T lo
@@ -474,6 +501,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_st_cols<kHalf>(tD, lv);
       tmem_wait_st();
       tc_fence_before();
+      if (threadIdx.x == 0) TF32_PROBE_ADD(5, e1);
       mbar_arrive(&bars->p_full[bb]);
     }
     if (ok && n > 0) ok = tc::warp_wait(&bars->acc_done, 0, ctl);

@@ -38,6 +38,18 @@ namespace sdpa_b200 {
 namespace tf32 {
 
 constexpr int kBM = 128;
+
+// Timing probe of tuning builds (-DSDPA_B200_TF32_FWD_PROBE): SM cycles of the
+// roles of CTA 0, summed into slots of g_tf32_fwd_probe.
+#ifdef SDPA_B200_TF32_FWD_PROBE
+__device__ unsigned long long g_tf32_fwd_probe[16];
+#define TF32F_T0(v) const long long v = clock64()
+#define TF32F_ADD(slot, t0) \
+  if (blockIdx.x == 0) atomicAdd(&g_tf32_fwd_probe[slot], static_cast<unsigned long long>(clock64() - (t0)))
+#else
+#define TF32F_T0(v)
+#define TF32F_ADD(slot, t0)
+#endif
 constexpr int kFwdThreads = 320;
 
 template <int DQK, int DV>
@@ -249,7 +261,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t sb = smem_u32(smem);
       auto issue_s = [&](int j) -> bool {
         const int s = j % NS;
+        TF32F_T0(a0);
         if (!mbar_wait(&bars->k_ready[s], (j / NS) & 1, ctl)) return false;
+        TF32F_ADD(0, a0);
+        TF32F_T0(a1);
         tc_fence_after();
         const uint32_t tS = tmem + Cfg::kS + (j & 1) * 2 * kBN;
 #pragma unroll
@@ -262,11 +277,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mma_tf32_ts(tS, tmem + Cfg::kQl + kk * 8, bh, idesc_s, 1u);
         }
         mma_commit(&bars->s_full[j & 1]);
+        TF32F_ADD(1, a1);
         return true;
       };
       auto issue_pv = [&](int t) -> bool {
         const int s = t % NS;
+        TF32F_T0(a2);
         if (!mbar_wait(&bars->p_full[t & 1], (t >> 1) & 1, ctl)) return false;
+        TF32F_ADD(2, a2);
+        TF32F_T0(a3);
         if (!mbar_wait(&bars->v_ready[s], (t / NS) & 1, ctl)) return false;
         tc_fence_after();
         const uint32_t tPh = tmem + Cfg::kS + (t & 1) * 2 * kBN, tPl = tPh + kBN;
@@ -281,6 +300,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mma_tf32_ts(tmem + Cfg::kO, tPl + kk * 8, vh, idesc_pv, 1u);
         }
         mma_commit(&bars->kv_empty[s]);
+        TF32F_ADD(3, a3);
         mma_commit(&bars->o_done);
         return true;
       };
@@ -309,13 +329,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int tid = threadIdx.x - 128;
     for (int j = 0; j < n_kv; ++j) {
       const int s = j % NS;
+      TF32F_T0(c0);
       if (!tc::warp_wait(&bars->k_full[s], (j / NS) & 1, ctl)) break;
+      if (tid == 0) TF32F_ADD(4, c0);
+      TF32F_T0(c1);
       split_tile(smem + Cfg::khi(s), smem + Cfg::klo(s), Cfg::kKBytes, tid, 128);
       fence_proxy_async_smem();
       mbar_arrive(&bars->k_ready[s]);
       if (!tc::warp_wait(&bars->v_full[s], (j / NS) & 1, ctl)) break;
       split_tile(smem + Cfg::vhi(s), smem + Cfg::vlo(s), Cfg::kVBytes, tid, 128);
       fence_proxy_async_smem();
+      if (tid == 0) TF32F_ADD(5, c1);
       mbar_arrive(&bars->v_ready[s]);
     }
   } else {
@@ -350,10 +374,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;  // TMEM tile buffer
+      TF32F_T0(e0);
       if (!tc::warp_wait(&bars->s_full[s], (j >> 1) & 1, ctl)) {
         ok = false;
         break;
       }
+      if (t == 0) TF32F_ADD(6, e0);
+      TF32F_T0(e1);
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + Cfg::kS + s * 2 * kBN;
       uint32_t r[kBN];
@@ -451,6 +478,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
+      if (t == 0) TF32F_ADD(7, e1);
       mbar_arrive(&bars->p_full[s]);
     }
     // ----------------------------------------------------------- epilogue

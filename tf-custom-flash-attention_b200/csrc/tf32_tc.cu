@@ -97,3 +97,21 @@ int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) 
 }
 
 SDPA_B200_STATUS_EXCHANGE(tf32)
+
+#ifdef SDPA_B200_TF32_PROBE
+// Reads and clears the timing probe of tuning builds.
+extern "C" int sdpa_b200_tf32_probe_read(unsigned long long* out) {
+  const unsigned long long zero[16] = {};
+  if (cudaMemcpyFromSymbol(out, tf32::g_tf32_probe, sizeof(zero)) != cudaSuccess) return 1;
+  return cudaMemcpyToSymbol(tf32::g_tf32_probe, zero, sizeof(zero)) == cudaSuccess ? 0 : 1;
+}
+#endif
+
+#ifdef SDPA_B200_TF32_FWD_PROBE
+// Reads and clears the forward timing probe of tuning builds.
+extern "C" int sdpa_b200_tf32_fwd_probe_read(unsigned long long* out) {
+  const unsigned long long zero[16] = {};
+  if (cudaMemcpyFromSymbol(out, tf32::g_tf32_fwd_probe, sizeof(zero)) != cudaSuccess) return 1;
+  return cudaMemcpyToSymbol(tf32::g_tf32_fwd_probe, zero, sizeof(zero)) == cudaSuccess ? 0 : 1;
+}
+#endif
