@@ -370,6 +370,8 @@ int sdpa_b200_bwd_noalloc(int dtype, const void* q, const void* k, const void* v
   t_launches = 0;
   if (int r = check_common(dtype, B, S_q, S_kv, D_qk, D_v, causal)) return r;
   if (B * S_q > SDPA_B200_NOALLOC_MAX_ROWS) return SDPA_B200_ESCRATCH;
+  // the symbol lookup and the launches must use the same (primary) context
+  if (int r = bind_context()) return r;
   void* scratch = noalloc_scratch_ptr();
   if (!scratch) return SDPA_B200_ECUDA;
   return sdpa_b200_bwd(dtype, q, k, v, out, stats, d_out, dq, dk, dv, B, S_q, S_kv, D_qk, D_v, scale, dropout,

@@ -18,10 +18,37 @@ constexpr int kFwdKeys = 32;   // keys per staged tile
 constexpr int kBwdRows = 64;   // rows owned per CTA in dkdv / dq
 constexpr int kBwdTile = 32;   // rows per staged tile of the other side
 
+// dst[r][d] (row-major, width DM) <- src rows row0.. (row stride ld; zero
+// outside).  Rows whose start and length are 16-byte multiples (and a 16-byte
+// aligned base) move in 16-byte vectors, one per thread per step, coalesced
+// along the row; others element by element.
 template <typename T>
 __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t ld, int64_t row0, int64_t nrows_total,
                                            int rows, int D, int DM, int tid, int nthreads) {
-  // dst[r][d] (row-major, width DM) <- src rows row0.. (row stride ld; zero outside)
+  constexpr int V = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte vector
+  const bool vec = (D % V == 0) && (ld % V == 0) && (DM % V == 0) &&
+                   ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  if (vec) {
+    const int per_row = DM / V;
+    for (int idx = tid; idx < rows * per_row; idx += nthreads) {
+      const int r = idx / per_row, d = (idx - r * per_row) * V;
+      const int64_t gr = row0 + r;
+      float f[V];
+      if (gr < nrows_total && d < D) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + gr * ld + d);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int i = 0; i < V; ++i) f[i] = to_f<T>(e[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) f[i] = 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < V; i += 4)
+        *reinterpret_cast<float4*>(dst + r * DM + d + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+    }
+    return;
+  }
   for (int idx = tid; idx < rows * DM; idx += nthreads) {
     int r = idx / DM, d = idx - r * DM;
     int64_t gr = row0 + r;
@@ -31,8 +58,8 @@ __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t ld,
 
 template <typename T, int DM>
 __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
-  __shared__ float Ks[kFwdKeys * DM];
-  __shared__ float Vs[kFwdKeys * DM];
+  __shared__ __align__(16) float Ks[kFwdKeys * DM];
+  __shared__ __align__(16) float Vs[kFwdKeys * DM];
   const int64_t n_qt = (p.S_q + kFwdRows - 1) / kFwdRows;
   const int64_t b = blockIdx.x % p.B;
   const int64_t qt = n_qt - 1 - blockIdx.x / p.B;  // heavy causal tiles first

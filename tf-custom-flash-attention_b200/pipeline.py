@@ -12,6 +12,8 @@ call: each chunk passes the offset rebased to its first batch row
 """
 from __future__ import annotations
 
+import threading
+
 import torch
 
 from . import _lib, ops, sharding
@@ -21,7 +23,8 @@ _SETS = 3  # chunks in flight: copy-in, compute, copy-out
 
 
 def _chunk_buffers(dev, dtype, nb, S_q, S_kv, D_qk, D_v):
-    key = (str(dev), dtype, nb, S_q, S_kv, D_qk, D_v)
+    # per thread: calls from two threads (on their own streams) must not share device buffers
+    key = (str(dev), dtype, nb, S_q, S_kv, D_qk, D_v, threading.get_ident())
     if key not in _buffers:
         def e(*shape, dt=dtype):
             return torch.empty(shape, dtype=dt, device=dev)
@@ -36,10 +39,17 @@ def _chunk_buffers(dev, dtype, nb, S_q, S_kv, D_qk, D_v):
 
 
 def train_step_host(q, k, v, d_o, seed, offset, *, scale=1.0, dropout=0.0, causal_mask=False, chunks=8,
-                    device=None, out=None):
+                    device=None, out=None, synchronize=False):
     """(o, stats, dq, dk, dv) on pinned host memory; q, k, v, d_o pinned host [B, S, D] tensors.
 
     `out` may pass preallocated pinned host tensors (o, stats, dq, dk, dv) to reuse across calls.
+    The call returns once the work is queued: the copies back to host memory
+    complete in stream order, and the caller's current stream waits for them.
+    Synchronize that stream (or pass synchronize=True) before reading the
+    returned tensors on the host.  Calls from one thread reuse one set of
+    device buffers, so they must be ordered on one stream (as they are when
+    made from the same thread without switching streams); calls from other
+    threads get their own buffers.
     """
     dev = torch.device(device or "cuda")
     B, S_q, D_qk = q.shape
@@ -90,4 +100,6 @@ def train_step_host(q, k, v, d_o, seed, offset, *, scale=1.0, dropout=0.0, causa
             done.record(d2h)
         copied_out.append(done)
     main.wait_event(copied_out[-1])
+    if synchronize:
+        copied_out[-1].synchronize()
     return out
