@@ -70,8 +70,24 @@ int launch_pair_fwd(const Params& p, cudaStream_t st, int* launches) {
                       : launch_pair_fwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
+// Paired tiles share every K/V tile between two 128-row query tiles, but
+// halve the number of CTAs.  With a causal mask and few batch rows (a batch
+// sharded over many GPUs) the paired grid is about one wave of CTAs of very
+// unequal length, and the one-tile kernel is faster (cfg4 rows on one GPU:
+// 4 rows 593 vs 397 TFLOP/s forward; 8 rows 686 vs 788 the other way round;
+// non-causal 16 x 2048 rows still favour pairs, 665 vs 549).  Causal problems
+// use pairs from pair_min_ctas() paired CTAs on.
+int64_t pair_min_ctas() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("SDPA_B200_FWD_PAIR_MIN_CTAS");
+    return e ? std::atoll(e) : static_cast<int64_t>(200);
+  }();
+  return v;
+}
+
 int tc_fwd_dispatch(const Params& p, cudaStream_t st, int* launches) {
-  if (!std::getenv("SDPA_B200_FWD_SINGLE")) {
+  const int64_t pair_ctas = ((p.S_q + 2 * tc::kBM - 1) / (2 * tc::kBM)) * p.B;
+  if (!std::getenv("SDPA_B200_FWD_SINGLE") && (!p.causal || pair_ctas >= pair_min_ctas())) {
     const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
     if (q128 && v128) return launch_pair_fwd<128, 128>(p, st, launches);
     if (q128) return launch_pair_fwd<128, 64>(p, st, launches);
