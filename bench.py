@@ -12,7 +12,8 @@ rows per GPU at N = 1/2/4/8), each rank's dropout offset rebased
 (sharding.shard_offset) so masks equal the unsharded run; no collective on the
 data path; time = max over ranks.  Outside the timed region the first row of
 every shard (o, stats, dq, dk, dv) is all-gathered over NCCL to rank 0, which
-recomputes those global rows alone and checks them bit for bit ("validated").
+rebuilds each shard from its per-row seeds, reruns it at the global offset and
+checks those rows bit for bit ("validated").
 The weak-scaling figure (every rank the full per-GPU batch) is reported beside
 it, as are each rank's pinned host<->device copy bandwidths measured alone and
 with all ranks copying at once (what bounds the end-to-end number).
@@ -345,7 +346,7 @@ def run_ours(args, w):
                  "reasons": clk.get("reasons")}]
 
     # ---- validation over NCCL (outside the timed region): the first row of every
-    # shard, recomputed alone on rank 0 with the global offset, must match bit for bit
+    # shard, recomputed on rank 0 with the global offset, must match bit for bit
     names = ("o", "s", "dq", "dk", "dv")
     sample = [last[n][0].contiguous() for n in names]
     if world > 1:
@@ -354,15 +355,18 @@ def run_ours(args, w):
             bufs = [torch.empty_like(t) for _ in range(world)]
             torch.distributed.all_gather(bufs, t)
             gathered.append(bufs)
-        starts = [fa.sharding.shard_rows(B_glob, world, r)[0] for r in range(world)]
+        shards = [fa.sharding.shard_rows(B_glob, world, r) for r in range(world)]
     else:
         gathered = [[t] for t in sample]
-        starts = [b0]
+        shards = [(b0, b1)]
+    starts = [a for a, _ in shards]
     validated, mismatched = None, []
     if rank == 0:
         validated = True
-        for r, gb in enumerate(starts):
-            rq, rk, rv, rdo = make_rows(w, gb, gb + 1, dev, dt)
+        for r, (gb, ge) in enumerate(shards):
+            # the shard rebuilt from its seeds and run with the shard's own batch size
+            # (the kernel choice depends on it), at the global offset of its first row
+            rq, rk, rv, rdo = make_rows(w, gb, ge, dev, dt)
             off_r = fa.sharding.shard_offset(w["offset"], gb, S, S_kv)
             step(rq, rk, rv, rdo, off_r, record=False)
             for n, bufs in zip(names, gathered):
@@ -487,7 +491,8 @@ def run_ours(args, w):
                 "bound": "pinned host<->device copies (see per_rank copy GB/s)"},
         "validated": validated, "validation": {"rows_checked": starts, "mismatches": mismatched,
                                                "method": "NCCL all_gather of each shard's first row; rank 0 "
-                                                         "recomputes it alone with the global offset; bit-exact"},
+                                                         "rebuilds that shard from its seeds, reruns it with the "
+                                                         "global offset and compares bit for bit"},
         "weak_scaling": weak,
         "gpu_launches": timed_launches,
         "per_rank": per_rank,
