@@ -62,6 +62,8 @@ FWD_CASES = [
     (np.float32, 2, 64, 64, 32, 4, False, 0.2),
     (np.float32, 2, 40, 136, 64, 128, False, 0.05),
     (np.float32, 2, 50, 50, 5, 3, True, 0.25),
+    (np.float32, 2, 150, 150, 64, 32, True, 0.1),      # 3xTF32, narrow values (D_v <= 32 kernels)
+    (np.float32, 1, 70, 300, 48, 20, False, 0.0),
 ]
 
 

@@ -378,10 +378,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if constexpr (Cfg::kHasY) {
         const void* ysrc = kRowsAreQueries ? p.d_o : p.v;
         const float* yrow = static_cast<const float*>(ysrc) + (row_ok ? row_offset_t<HEADS>(p.H, b, rr, S_res, p.D_v) : 0);
+        constexpr int HC = DV / 2 < 32 ? 32 : DV / 2;  // columns per half (D_v = 32: half 0 takes all)
+        if (half * HC < DV) {
 #pragma unroll
-        for (int c = 0; c < DV / 64; ++c) {
-          const int cc = half * (DV / 2) + c * 32;
-          row_to_tmem(yrow, cc, p.D_v, row_ok, tmem + lane_base + Cfg::kYh + cc, tmem + lane_base + Cfg::kYl + cc);
+          for (int c = 0; c < HC / 32; ++c) {
+            const int cc = half * HC + c * 32;
+            row_to_tmem(yrow, cc, p.D_v, row_ok, tmem + lane_base + Cfg::kYh + cc, tmem + lane_base + Cfg::kYl + cc);
+          }
         }
       }
       tmem_wait_st();
@@ -528,8 +531,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       } else {
-        store_acc_row_f32(tmem + lane_base + Cfg::kAcc + half * (DA / 2), DA / 64, half * (DA / 2), 1.0f, n > 0,
-                          row_ok, drow, D);
+        constexpr int HC = DA / 2 < 32 ? 32 : DA / 2;  // columns per half (D_v = 32: half 0 takes all)
+        if (half * HC < DA)
+          store_acc_row_f32(tmem + lane_base + Cfg::kAcc + half * HC, HC / 32, half * HC, 1.0f, n > 0, row_ok, drow,
+                            D);
       }
     }
   }

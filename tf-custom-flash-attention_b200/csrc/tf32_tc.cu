@@ -86,6 +86,10 @@ int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) 
   if (q128 && v128) return SDPA_B200_EUNSUPPORTED;
   if (q128) return launch_fwd_d<128, 64>(p, st, launches);
   if (v128) return launch_fwd_d<64, 128>(p, st, launches);
+#ifndef SDPA_B200_TF32_NARROW_FWD
+#define SDPA_B200_TF32_NARROW_FWD 1
+#endif
+  if (SDPA_B200_TF32_NARROW_FWD && p.D_v <= 32) return launch_fwd_d<64, 32>(p, st, launches);  // N = 32 output MMAs
   return launch_fwd_d<64, 64>(p, st, launches);
 }
 
@@ -93,6 +97,7 @@ int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) 
 // and accumulators of the DQ pass exceed TMEM.
 int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
   if (p.D_v > 64) return launch_bwd_d<64, 128>(p, st, launches);
+  if (p.D_v <= 32) return launch_bwd_d<64, 32>(p, st, launches);
   return launch_bwd_d<64, 64>(p, st, launches);
 }
 
