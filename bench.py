@@ -301,23 +301,33 @@ def run_ours(args, w):
         last.update(o=o, s=s, dq=dq, dk=dk, dv=dv)
         return e_mid
 
-    def timed_loop(q, k, v, do, off, steps, record=True):
+    in_bytes = sum(x.numel() * x.element_size() for x in (q, k, v, do))
+    # inputs that fit in L2 (126 MB): a 256 MB write between timed steps evicts them
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if in_bytes <= 126e6 else None
+
+    def timed_loop(q, k, v, do, off, steps, record=True, graph=None):
+        """Sum over `steps` of the device time of one step (events around each step on
+        the launching stream; the L2 flush, when used, runs between steps, untimed)."""
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
         evs = []
-        e0 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        prev = e0
         for _ in range(steps):
-            mid = step(q, k, v, do, off, record)
+            if flush_buf is not None:
+                flush_buf.zero_()
+            start = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            if graph is not None:
+                graph.replay()
+                mid = start
+            else:
+                mid = step(q, k, v, do, off, record)
             end = torch.cuda.Event(enable_timing=True)
             end.record(stream)
-            evs.append((prev, mid, end))
-            prev = end
+            evs.append((start, mid, end))
         torch.cuda.synchronize()
-        return e0.elapsed_time(prev), evs
+        return sum(a.elapsed_time(e) for a, _, e in evs), evs
 
     def max_over_ranks(x):
         if world == 1:
@@ -334,9 +344,24 @@ def run_ours(args, w):
     kev.clear()
     total_ms, evs = timed_loop(q, k, v, do, offset, args.steps)
     timed_launches = launches[0]
-    clk = clocks.stop()
     fwd_ms = sum(a.elapsed_time(m) for a, m, _ in evs) / args.steps
     bwd_ms = sum(m.elapsed_time(e) for _, m, e in evs) / args.steps
+    graph_ms = None
+    if not args.no_graph:
+        # The same step captured once in a CUDA graph and replayed: the timed
+        # work is unchanged (every kernel of every step runs), the host-side
+        # launch cost (Python, argument checks, TMA descriptor encoding) is
+        # taken out, which is what bounds short steps.
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            o_, s_ = fa.sdpa(q, k, v, w["seed"], offset, **kw)
+            fa.sdpa_grad(q, k, v, o_, s_, do, w["seed"], offset, **kw)
+        for _ in range(2):
+            g.replay()
+        graph_ms, _ = timed_loop(q, k, v, do, offset, args.steps, graph=g)
+        total_ms = graph_ms
+        del g
+    clk = clocks.stop()
     kernel_ms = None
     if knames and len(kev) == args.steps:
         kernel_ms = {name: sum(e[i].elapsed_time(e[i + 1]) for e in kev) / args.steps for i, name in enumerate(knames)}
@@ -471,7 +496,6 @@ def run_ours(args, w):
             cpu = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample_txt}
         except Exception as e:  # the reference build is missing on this box
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
-    in_bytes = sum(x.numel() * x.element_size() for x in (q, k, v, do))
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -479,8 +503,10 @@ def run_ours(args, w):
         "config": {"workload": args.workload, "global_batch": B_glob, "per_gpu_batch": B, "seq_len": S,
                    "seq_len_kv": S_kv, "D_qk": Dq, "D_v": Dv, "causal": w["causal"], "dropout": w["dropout"],
                    "parallelism": f"batch-sharded x{world} (strong scaling), no collective on the data path",
+                   "cuda_graph": not args.no_graph,
                    "l2": f"inputs {in_bytes / 1e6:.0f} MB per rank per step "
-                         + ("(larger than L2)" if in_bytes > 126e6 else "(fit in L2: small config)")},
+                         + ("(larger than L2)" if flush_buf is None else
+                            "(fit in L2: a 256 MB write flushes L2 between timed steps)")},
         "kernel_path": path,
         "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf, "pct_of_peak": 100.0 * value / world / peak,
         "roofline": {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
@@ -494,7 +520,7 @@ def run_ours(args, w):
                                                          "rebuilds that shard from its seeds, reruns it with the "
                                                          "global offset and compares bit for bit"},
         "weak_scaling": weak,
-        "gpu_launches": timed_launches,
+        "gpu_launches": timed_launches,  # per step x steps (the graph replays the same launches)
         "per_rank": per_rank,
         "clocks": clk,
         "cpu_baseline": cpu,
@@ -516,6 +542,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time the eager launches instead of a CUDA graph replay")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (small profiling runs)")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
