@@ -429,7 +429,7 @@ def run_ours(args, w):
         nonlocal outs_h, d2h
         outs_h = fa.pipeline.train_step_host(hq, hk, hv, hdo, w["seed"], offset, scale=kw["scale"],
                                              dropout=kw["dropout"], causal_mask=kw["causal_mask"],
-                                             chunks=min(8, B), device=dev, out=outs_h)
+                                             chunks=min(16, B), device=dev, out=outs_h)
         d2h = sum(x.numel() * x.element_size() for x in outs_h)
 
     e2e_steps = max(1, min(args.steps, 5))
