@@ -143,3 +143,17 @@ def test_mha_training_offset_advances_between_calls(layout):
         else:
             expect = o3.view(shape[0], shape[2], H, S, dh).permute(0, 3, 1, 2, 4).reshape(shape)
         assert torch.equal(out, expect), n
+
+
+def test_fp32_runs_on_the_tensor_core_kernels():
+    """cfg5's fp32 shapes take the 3xTF32 tcgen05 kernels (one forward launch,
+    three backward passes), not the SIMT fallback."""
+    assert fa.kernel_path(torch.float32, 64, 128) == "tcgen05-3xtf32"
+    assert fa.kernel_path(torch.float32, 64, 128, backward=True) == "tcgen05-3xtf32"
+    q, k, v, do, kw = cfg5_inputs(B=1)
+    tq, tk, tv, tdo = cuda(q, k, v, do)
+    o, s = fa.sdpa(tq, tk, tv, 0, 0, **kw)
+    assert fa.last_launch_count() == 1
+    fa.sdpa_grad(tq, tk, tv, o, s, tdo, 0, 0, **kw)
+    assert fa.last_launch_count() == 3
+    torch.cuda.synchronize()
