@@ -38,6 +38,8 @@ def test_path_selection():
     assert fa.kernel_path(torch.float16, 128, 128) == "tcgen05"
     assert fa.kernel_path(torch.float16, 64, 40) == "tcgen05"
     assert fa.kernel_path(torch.float16, 5, 3) == "simt"
+    assert fa.kernel_path(torch.float16, 8, 64) == "simt"      # too few dims: the reference's product rounding
+    assert fa.kernel_path(torch.float16, 16, 8) == "tcgen05"
     assert fa.kernel_path(torch.float32, 64, 128) == "tcgen05-3xtf32"
     assert fa.kernel_path(torch.float32, 32, 4, backward=True) == "tcgen05-3xtf32"
     assert fa.kernel_path(torch.float32, 128, 64) == "tcgen05-3xtf32"

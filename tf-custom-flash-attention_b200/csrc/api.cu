@@ -88,17 +88,22 @@ int check_common(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, 
   return SDPA_B200_OK;
 }
 
+// fp16 scores over fewer than 16 dims stay on the SIMT kernels, which round
+// each q*k product to half before summing as the reference does: over so few
+// terms that rounding is a visible part of its result (a sweep of random
+// shapes found D_qk = 8 on the tensor cores 2.2e-3 of max from the reference).
 bool tc_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
                const void* o) {
   if (force_simt() || dtype != SDPA_B200_F16) return false;
   if (S_kv == 0) return false;  // a TMA map cannot have a zero extent
   if (D_qk % 8 != 0 || D_v % 8 != 0) return false;  // TMA row strides must be 16-byte multiples
+  if (D_qk < 16) return false;  // see the comment above
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
 }
 
 bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n) {
   if (force_simt() || dtype != SDPA_B200_F16 || S_q == 0 || S_kv == 0) return false;
-  if (D_qk % 8 != 0 || D_v % 8 != 0) return false;
+  if (D_qk % 8 != 0 || D_v % 8 != 0 || D_qk < 16) return false;  // D_qk < 16: see tc_fwd_ok
   for (int i = 0; i < n; ++i)
     if (!aligned16(ptrs[i])) return false;
   return true;
@@ -313,7 +318,7 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
   if (force_simt()) return 0;
-  if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0) ? 1 : 0;
+  if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0 && D_qk >= 16) ? 1 : 0;
   if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (backward ? D_qk <= 64 : (D_qk <= 64 || D_v <= 64)))
     return 2;
   return 0;

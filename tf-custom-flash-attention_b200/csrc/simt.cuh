@@ -56,6 +56,22 @@ __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t ld,
   }
 }
 
+// acc + a*b as the reference's `score += T(a*b)`: for half the product is
+// rounded to half before the fp32 sum (Eigen::half arithmetic,
+// sdpa/sdpa_fwd.cu.cc:108, sdpa/sdpa_bwd.cu.cc:98, 128, 154); for float a fused
+// multiply-add.  On these kernels' small head dims (rows that are not 16-byte
+// multiples) the rounding is a visible part of the reference's result.
+template <typename T>
+__device__ __forceinline__ float dot_step(float acc, float a, float b);
+template <>
+__device__ __forceinline__ float dot_step<float>(float acc, float a, float b) {
+  return fmaf(a, b, acc);
+}
+template <>
+__device__ __forceinline__ float dot_step<__half>(float acc, float a, float b) {
+  return acc + __half2float(__float2half_rn(a * b));
+}
+
 template <typename T, int DM>
 __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
   __shared__ __align__(16) float Ks[kFwdKeys * DM];
@@ -75,7 +91,8 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
   float qr[DM], acc[DM];
 #pragma unroll
   for (int d = 0; d < DM; ++d) {
-    qr[d] = (active && d < p.D_qk) ? to_f<T>(Q[row * ldqk + d]) * p.scale_log2 : 0.0f;
+    // float: scale folded into q; half: products of the raw values, scaled after the sum
+    qr[d] = (active && d < p.D_qk) ? to_f<T>(Q[row * ldqk + d]) * (sizeof(T) == 2 ? 1.0f : p.scale_log2) : 0.0f;
     acc[d] = 0.0f;
   }
   float m = -INFINITY, l = 0.0f;
@@ -96,7 +113,8 @@ __global__ void __launch_bounds__(kFwdRows) fwd_kernel(Params p) {
       const bool valid = j < p.S_kv && (!p.causal || j <= row);
       float s = 0.0f;
 #pragma unroll
-      for (int d = 0; d < DM; ++d) s = fmaf(qr[d], Ks[jj * DM + d], s);
+      for (int d = 0; d < DM; ++d) s = dot_step<T>(s, qr[d], Ks[jj * DM + d]);
+      if (sizeof(T) == 2) s *= p.scale_log2;
       sc[jj] = valid ? s : -INFINITY;
       tmax = fmaxf(tmax, sc[jj]);
     }
@@ -137,7 +155,7 @@ __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   const T* dO = static_cast<const T*>(p.d_o) + off;
   const T* O = static_cast<const T*>(p.o) + off;
   float s = 0.0f;
-  for (int d = lane; d < p.D_v; d += 32) s = fmaf(to_f<T>(dO[d]), to_f<T>(O[d]), s);
+  for (int d = lane; d < p.D_v; d += 32) s = dot_step<T>(s, to_f<T>(dO[d]), to_f<T>(O[d]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   // A gradient g_i reaching stats_i = logsumexp adds g_i * p_ij to dS_ij,
@@ -224,9 +242,9 @@ __global__ void __launch_bounds__(kBwdRows * dkdv_split<DM>()) dkdv_kernel(Param
       if (p.causal && i < kv) continue;
       float s = 0.0f, dP = 0.0f;
 #pragma unroll
-      for (int d = 0; d < DH; ++d) s = fmaf(Qs[rr * DM + d0 + d], Kt[(d0 + d) * kBwdRows + r], s);
+      for (int d = 0; d < DH; ++d) s = dot_step<T>(s, Qs[rr * DM + d0 + d], Kt[(d0 + d) * kBwdRows + r]);
 #pragma unroll
-      for (int d = 0; d < DH; ++d) dP = fmaf(dOs[rr * DM + d0 + d], Vt[(d0 + d) * kBwdRows + r], dP);
+      for (int d = 0; d < DH; ++d) dP = dot_step<T>(dP, dOs[rr * DM + d0 + d], Vt[(d0 + d) * kBwdRows + r]);
       if (SPLIT == 2) {
         // Only the two threads of this key row are guaranteed to be here (rows
         // of a warp skip different query rows), so the shuffle names just them.
@@ -299,9 +317,9 @@ __global__ void __launch_bounds__(kBwdRows) dq_kernel(Params p) {
       if (p.causal && j > row) break;
       float s = 0.0f, dP = 0.0f;
 #pragma unroll
-      for (int d = 0; d < DM; ++d) s = fmaf(Qt[d * kBwdRows + tid], Ks[jj * DM + d], s);
+      for (int d = 0; d < DM; ++d) s = dot_step<T>(s, Qt[d * kBwdRows + tid], Ks[jj * DM + d]);
 #pragma unroll
-      for (int d = 0; d < DM; ++d) dP = fmaf(dOt[d * kBwdRows + tid], Vs[jj * DM + d], dP);
+      for (int d = 0; d < DM; ++d) dP = dot_step<T>(dP, dOt[d * kBwdRows + tid], Vs[jj * DM + d]);
       float pr, dS;
       if (!elem_grad(p, s * p.scale_log2, lse2, delta, lcg_state(rbase, static_cast<uint64_t>(j)), dP, pr, dS))
         continue;

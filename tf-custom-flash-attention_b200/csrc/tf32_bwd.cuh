@@ -91,6 +91,7 @@ struct BwdBarriers {
   uint64_t st_full[3], st_ready[3], st_empty[3];
   uint64_t s_full[2], p_full[2];
   uint64_t acc_done, mma_done;
+  uint64_t acc_step;  // DV: the accumulating MMAs of a tile completed
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -214,6 +215,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(&bars->acc_done, 1);
     mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->acc_step, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -301,8 +303,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!mbar_wait(&bars->p_full[bb], (t >> 1) & 1, ctl)) return false;
           tc_fence_after();
           const uint32_t buf = tT + bb * 2 * kN;
-          issue_acc<DV, kN>(tmem + Cfg::kAcc, buf, buf + kN, sb + Cfg::sb_hi(s), sb + Cfg::sb_lo(s), t == 0);
+          // fresh accumulator every tile, folded into the elementwise threads' total
+          issue_acc<DV, kN>(tmem + Cfg::kAcc, buf, buf + kN, sb + Cfg::sb_hi(s), sb + Cfg::sb_lo(s), true);
           mma_commit(&bars->st_empty[s]);
+          mma_commit(&bars->acc_step);
           return true;
         };
         for (int t = 0; ok && t < n; ++t) {
@@ -417,10 +421,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // of MMAs (dQ over S_kv = 4096 keys) its error reaches a few 1e-5.  So
     // each tile's products go to a fresh accumulator, folded in here in fp32:
     // s_full(t) is committed after acc(t-1) was issued, so it is complete.
+    // DV: the same, with the total of this thread's kTotCols columns of dV,
+    // folded at the end of every tile after acc_step shows the previous tile's
+    // accumulating MMAs complete (the next tile's restart the accumulator).
     static_assert(!Cfg::kHasY || Cfg::kAccCols == 64, "running total sized for D_qk = 64");
-    float tot[32];
+    constexpr int kTotCols = Cfg::kHasY ? 32 : (DV / 2 < 32 ? 32 : DV / 2);
+    const bool has_cols = Cfg::kHasY || half * kTotCols < DV;  // D_v = 32: half 1 holds none
+    float tot[kTotCols];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) tot[e] = 0.0f;
+    for (int e = 0; e < kTotCols; ++e) tot[e] = 0.0f;
     bool ok = true;
     for (int t = 0; t < n; ++t) {
       const int s = t % kStages;
@@ -502,6 +511,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_st_cols<kHalf>(tS, hv);
       tmem_st_cols<kHalf>(tD, lv);
+      if (!Cfg::kHasY && t > 0 && has_cols) {
+        // acc_step is waited every tile by these warps, so never two phases behind
+        if (!tc::warp_wait(&bars->acc_step, (t - 1) & 1, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kTotCols / 32; ++c) {
+          uint32_t a[32];
+          SDPA_TMEM_LD32(tmem + lane_base + Cfg::kAcc + half * kTotCols + c * 32, a);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) tot[c * 32 + e] += __uint_as_float(a[e]);
+        }
+      }
       tmem_wait_st();
       tc_fence_before();
       if (threadIdx.x == 0) TF32_PROBE_ADD(5, e1);
@@ -531,10 +556,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       } else {
-        constexpr int HC = DA / 2 < 32 ? 32 : DA / 2;  // columns per half (D_v = 32: half 0 takes all)
-        if (half * HC < DA)
-          store_acc_row_f32(tmem + lane_base + Cfg::kAcc + half * HC, HC / 32, half * HC, 1.0f, n > 0, row_ok, drow,
-                            D);
+        if (has_cols) {
+#pragma unroll
+          for (int c = 0; c < kTotCols / 32; ++c) {
+            uint32_t a[32];
+            if (n > 0) {
+              SDPA_TMEM_LD32(tmem + lane_base + Cfg::kAcc + half * kTotCols + c * 32, a);
+              tmem_wait_ld();
+            }
+            if (row_ok) {
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const int col = half * kTotCols + c * 32 + 4 * g;
+                float v4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  v4[e] = tot[c * 32 + 4 * g + e] + (n > 0 ? __uint_as_float(a[4 * g + e]) : 0.0f);
+                if (col < D) *reinterpret_cast<float4*>(drow + col) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+              }
+            }
+          }
+        }
       }
     }
   }
