@@ -276,8 +276,14 @@ def run_ours(args, w):
     stream = torch.cuda.current_stream()
     path = fa.kernel_path(dt, Dq, Dv, backward=True)
     # per-kernel timing of the backward on the launching stream, through the
-    # library's diagnostic event hook: fp16 runs dQ then dK/dV, fp32 dQ, dK, dV
-    knames = {"tcgen05": ("dq2_kernel", "dkdv_kernel"), "tcgen05-3xtf32": ("tf32 dQ", "tf32 dK", "tf32 dV")}.get(path)
+    # library's diagnostic event hook: fp16 runs dQ then dK/dV; fp32 either the
+    # GEMM route (D + the DK pass writing dS and P~^T, then the dQ and dV GEMMs,
+    # when the workspace query asks for room for them) or the passes dQ, dK, dV
+    tf32_gemm = (dt == torch.float32 and fa._lib.lib().sdpa_b200_bwd_workspace_bytes(
+        fa._lib.F32, B, S, S_kv, Dq, Dv) > B * S * 4)
+    knames = {"tcgen05": ("dq2_kernel", "dkdv_kernel"),
+              "tcgen05-3xtf32": (("tf32 D + dK pass", "tf32 dQ gemm", "tf32 dV gemm") if tf32_gemm
+                                 else ("tf32 dQ", "tf32 dK", "tf32 dV"))}.get(path)
     launches = [0]
     kev = []
     last = {}
@@ -472,9 +478,10 @@ def run_ours(args, w):
     if kernel_ms and path == "tcgen05":
         cands += [("dkdv_kernel", kernel_ms["dkdv_kernel"], unit * (2 * Dq + 2 * Dv)),
                   ("dq2_kernel", kernel_ms["dq2_kernel"], unit * Dq)]
-    elif kernel_ms:
-        cands += [("tf32 dQ", kernel_ms["tf32 dQ"], unit * Dq), ("tf32 dK", kernel_ms["tf32 dK"], unit * (2 * Dq + Dv)),
-                  ("tf32 dV", kernel_ms["tf32 dV"], unit * Dv)]
+    elif kernel_ms:  # fp32: the dK pass carries S, dP, dK; dQ and dV one product each, on either route
+        share = {"tf32 dQ": Dq, "tf32 dK": 2 * Dq + Dv, "tf32 dV": Dv,
+                 "tf32 D + dK pass": 2 * Dq + Dv, "tf32 dQ gemm": Dq, "tf32 dV gemm": Dv}
+        cands += [(n, kernel_ms[n], unit * share[n]) for n in knames]
     else:
         cands += [("bwd (all kernels)", bwd_ms, mf_bwd)]
     name, kms, kfl = max(cands, key=lambda c: c[1])

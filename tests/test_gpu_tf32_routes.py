@@ -1,0 +1,86 @@
+"""The two routes of the fp32 (3xTF32) backward, both against the oracle
+(needs a B200).
+
+* GEMM route (the workspace sdpa_b200_bwd_workspace_bytes asks for): D, the
+  DK pass writing dS and P~^T, then dQ = scale dS K and dV = P~^T dO as GEMMs
+  (4 launches).
+* Recomputing route (a workspace of one float per query row, as the
+  reference's op allocates): DQ, DK and DV passes (3 launches).
+
+Tolerance (north star): fp32 max|new - ref| <= 1e-5 * max|ref|.
+"""
+import importlib
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import cpu  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+fa = importlib.import_module("tf-custom-flash-attention_b200")
+
+
+def rel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def bwd(q, k, v, o, s, do, kw, minimal):
+    L = fa._lib.lib()
+    B, S_q, D_qk = q.shape
+    S_kv, D_v = k.shape[1], v.shape[2]
+    full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, D_qk, D_v)
+    n = B * S_q * 4 if minimal else full
+    assert minimal or full > B * S_q * 4  # the GEMM route applies to these shapes
+    ws = torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    rc = L.sdpa_b200_bwd(fa._lib.F32, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), s.data_ptr(),
+                         do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
+                         kw["scale"], kw["dropout"], int(kw["causal_mask"]), 5, 9, ws.data_ptr(), n,
+                         torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, fa._lib.strerror(rc)
+    launches = fa.last_launch_count()
+    torch.cuda.synchronize()
+    return [x.cpu().numpy() for x in (dq, dk, dv)], launches
+
+
+@pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
+    (2, 150, 150, 64, 32, True, 0.1),
+    (1, 70, 300, 48, 20, False, 0.0),
+    (2, 256, 640, 64, 128, False, 0.05),
+    (2, 384, 384, 32, 64, True, 0.0),
+    (3, 129, 33, 16, 100, False, 0.5),
+])
+def test_both_routes_match_oracle(B, S_q, S_kv, D_qk, D_v, causal, p):
+    rng = np.random.default_rng(S_q + 3 * S_kv + D_v)
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    do = rng.standard_normal((B, S_q, D_v)).astype(np.float32)
+    kw = dict(scale=D_qk ** -0.5, dropout=p, causal_mask=causal)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+    t = [torch.from_numpy(x).cuda() for x in (q, k, v, o_ref, s_ref, do)]
+    gemm, n_gemm = bwd(*t, kw, minimal=False)
+    passes, n_passes = bwd(*t, kw, minimal=True)
+    assert (n_gemm, n_passes) == (4, 3)
+    for route, got in (("gemm", gemm), ("passes", passes)):
+        for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
+            assert rel(a, b) <= 1e-5, (route, name, rel(a, b))
+    assert fa.device_status() == 0
+
+
+def test_workspace_query_sizes_the_gemm_route():
+    """fp32 shapes the route serves ask for dS and P~^T; fp16 and shapes over
+    the cap ask for one float per query row."""
+    L = fa._lib.lib()
+    B, S_q, S_kv = 2, 100, 70
+    full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 64, 128)
+    assert full >= B * S_q * 4 + B * S_q * 72 * 4 + B * S_kv * 128 * 4
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F16, B, S_q, S_kv, 64, 128) == B * S_q * 4
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) == B * S_q * 4
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4

@@ -202,9 +202,28 @@ int sdpa_b200_fwd_bshd(int dtype, const void* q, const void* k, const void* v, v
                   stream);
 }
 
-size_t sdpa_b200_bwd_workspace_bytes(int, int64_t B, int64_t S_q, int64_t, int64_t, int64_t) {
+// Workspace of the fp32 backward's GEMM route beyond the delta rows: dS
+// [B, S_q, ld_ds] and P~^T [B, S_kv, ld_p] (ld_p covers every column the DK
+// pass's tiles write), or 0 where the route does not apply.  Capped so that
+// the workspace stays a small part of HBM; above the cap (and with a smaller
+// workspace) the three recomputing passes run instead.
+constexpr size_t kGemmWorkspaceCap = size_t(4) << 30;
+static int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+static size_t delta_bytes(int64_t B, int64_t S_q) {
+  return static_cast<size_t>(round_up(B * S_q * static_cast<int64_t>(sizeof(float)), 256));
+}
+static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
+  if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
+  if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return 0;
+  const size_t ds = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
+  const size_t pt = static_cast<size_t>(round_up(B * S_kv * round_up(S_q, 64) * 4, 256));
+  return ds + pt <= kGemmWorkspaceCap ? ds + pt : 0;
+}
+
+size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
   if (B <= 0 || S_q <= 0) return 0;
-  return static_cast<size_t>(B) * static_cast<size_t>(S_q) * sizeof(float);
+  const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
+  return extra ? delta_bytes(B, S_q) + extra : static_cast<size_t>(B) * static_cast<size_t>(S_q) * sizeof(float);
 }
 
 static int bwd_impl(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
@@ -215,7 +234,8 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (int r = check_common(dtype, B, S_q, S_kv, D_qk, D_v, causal)) return r;
   if (H < 1 || B % H != 0) return SDPA_B200_EINVAL;
   if (B == 0 || (S_q == 0 && S_kv == 0)) return SDPA_B200_OK;
-  const size_t need = sdpa_b200_bwd_workspace_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
+  // one float per query row is required; the fp32 GEMM route uses more when given
+  const size_t need = (B > 0 && S_q > 0) ? static_cast<size_t>(B) * static_cast<size_t>(S_q) * sizeof(float) : 0;
   if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u)))
     return SDPA_B200_EWORKSPACE;
   if ((S_q > 0 && (!q || !out || !stats || !d_out || !dq)) || (S_kv > 0 && (!k || !v || !dk || !dv)))
@@ -237,7 +257,17 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (int r = bind_context()) return r;
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
-  if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tf32(p, st, &t_launches);
+  if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) {
+    const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
+    if (extra && workspace_bytes >= delta_bytes(B, S_q) + extra && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
+      uint8_t* w = static_cast<uint8_t*>(workspace) + delta_bytes(B, S_q);
+      p.ld_ds = round_up(S_kv, 4);
+      p.ld_p = round_up(S_q, 64);
+      p.ws_ds = reinterpret_cast<float*>(w);
+      p.ws_p = reinterpret_cast<float*>(w + round_up(B * S_q * p.ld_ds * 4, 256));
+    }
+    return launch_bwd_tf32(p, st, &t_launches);
+  }
   return dtype == SDPA_B200_F16 ? launch_bwd_simt_f16(p, st, &t_launches) : launch_bwd_simt_f32(p, st, &t_launches);
 }
 

@@ -98,6 +98,23 @@ inline bool make_map_f32_mn(CUtensorMap* m, const void* base, int64_t B, int64_t
   return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, B, H, S, D, rows, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
+// fp32 matrices [B, M, ld] (row length K <= ld, ld a multiple of 4) as the
+// 3-D map (column, row, batch), box 32 columns x `rows` rows, 128B swizzle;
+// columns beyond K and rows beyond M read as zero.
+inline bool make_map_rows_f32(CUtensorMap* m, const float* base, int64_t B, int64_t M, int64_t K, int64_t ld,
+                              int rows) {
+  auto fn = encode_fn();
+  if (!fn) return map_failure(0, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(M * ld) * 4};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
+}
+
 // Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
 template <typename K>
 inline cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done_mask) {

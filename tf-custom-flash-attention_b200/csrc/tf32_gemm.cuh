@@ -1,0 +1,271 @@
+// fp32 backward, second stage: dQ and dV as plain 3xTF32 GEMMs over the
+// score-shaped gradients the DK pass materialised (tf32_bwd.cuh, WS = true):
+//
+//   dQ[b] = scale * dS[b] K[b]        M = S_q rows, K-dim = S_kv
+//   dV[b] =         P~^T[b] dO[b]     M = S_kv rows, K-dim = S_q
+//
+// with dS = P (kf dP - D) and P~ = kf P, exactly the matrices the reference's
+// dQ and dK/dV kernels form element by element (sdpa/sdpa_bwd.cu.cc:125-170).
+// Recomputing them per pass (S, dP for dQ; S for dV) costs the fp32 path more
+// tensor time than reading them back: every recomputed product is three tf32
+// MMAs, and with hi / lo operands resident the recomputing passes only fit
+// N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
+//
+// One CTA = 128 rows of the result, all N columns.  Streams K-dim tiles of 32:
+// the A tile (128 x 32, K-major, 128-byte swizzle) and the B tile (32 x N,
+// MN-major, 32-byte swizzle atoms), both split in place into tf32 hi / lo by
+// four converter warps; one thread issues 4 x 3 SS MMAs per tile into one of
+// two TMEM accumulators, which 8 epilogue warps fold into an fp32 running
+// total every tile (the tensor cores' accumulation is not round-to-nearest).
+// Causal ranges: dQ row tile m0 needs keys < m0 + 128, dV row tile m0 queries
+// >= m0; every entry inside those ranges was written (masked ones as zero).
+#pragma once
+#include "common.cuh"
+#include "fwd_tc.cuh"
+#include "ptx.cuh"
+#include "tf32_fwd.cuh"
+
+namespace sdpa_b200 {
+namespace tf32 {
+
+constexpr int kGemmThreads = 448;
+
+struct GemmArgs {
+  float* c;          // result [B/H, M, H, D] (H = 1: [B, M, D])
+  int64_t B, H, M, K;
+  int D;             // result columns (<= N)
+  float alpha;
+  int range;         // 0: whole K-dim, 1: K-dim < m0 + 128 (dQ, causal), 2: K-dim >= m0 (dV, causal)
+  uint64_t timeout_ns;
+};
+
+template <int N>
+struct GemmCfg {
+  static constexpr int kK = 32;                          // K-dim per tile (one 128-byte row)
+  static constexpr uint32_t kABytes = 128 * kK * 4;      // 16 KB
+  static constexpr uint32_t kBBytes = kK * N * 4;        // N / 32 boxes of 32 x 32
+  static constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kStages = 4 * kStageBytes <= 200 * 1024 ? 4 : 3;
+  static constexpr uint32_t kBarOff = kStages * kStageBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * N < 32 ? 32 : 2 * N;  // two accumulators
+  static constexpr int kHC = N / 2;                      // columns per epilogue thread
+  static_assert(N == 32 || N == 64 || N == 128, "N");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static __device__ __forceinline__ uint32_t a_hi(int s) { return s * kStageBytes; }
+  static __device__ __forceinline__ uint32_t a_lo(int s) { return s * kStageBytes + kABytes; }
+  static __device__ __forceinline__ uint32_t b_hi(int s) { return s * kStageBytes + 2 * kABytes; }
+  static __device__ __forceinline__ uint32_t b_lo(int s) { return s * kStageBytes + 2 * kABytes + kBBytes; }
+};
+
+struct GemmBarriers {
+  uint64_t st_full[4], st_ready[4], st_empty[4];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int N>
+__device__ __forceinline__ void gemm_tmem_ld(uint32_t taddr, uint32_t* r) {
+  if constexpr (N == 16) {
+    SDPA_TMEM_LD16(taddr, r);
+  } else {
+    SDPA_TMEM_LD32(taddr, r);
+  }
+}
+
+// tm_a: 3-D map (K-dim, row, batch) of the materialised matrix, box 32 x 128.
+// tm_b: MN-major map (32-byte atoms) of K or dO, box 32 columns x 32 rows.
+template <int N, bool HEADS>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
+  using Cfg = GemmCfg<N>;
+  constexpr int kK = Cfg::kK, kStages = Cfg::kStages, kHC = Cfg::kHC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = tc::align1024(smem_raw);
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + Cfg::kBarOff);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+
+  const int64_t n_mt = (g.M + 127) / 128;
+  int64_t b, tord;
+  raster(blockIdx.x, g.B, n_mt, b, tord);
+  const int hb = HEADS ? static_cast<int>(b % g.H) : 0, ob = HEADS ? static_cast<int>(b / g.H) : static_cast<int>(b);
+  // heaviest causal row tiles first: high ones for dQ, low ones for dV
+  const int64_t m0 = (g.range == 1 ? n_mt - 1 - tord : tord) * 128;
+  const int64_t n_all = (g.K + kK - 1) / kK;
+  int tile0 = 0, n = static_cast<int>(n_all);
+  if (g.range == 1) {
+    n = static_cast<int>(min(n_all, (m0 + 127) / kK + 1));
+  } else if (g.range == 2) {
+    tile0 = static_cast<int>(m0 / kK);
+    n = static_cast<int>(n_all - tile0 > 0 ? n_all - tile0 : 0);
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->st_full[s], 1);
+      mbar_init(&bars->st_ready[s], 128);
+      mbar_init(&bars->st_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->acc_full[s], 1);
+      mbar_init(&bars->acc_empty[s], 256);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 13) tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  WaitCtl ctl;
+  ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;
+  ctl.abort_flag = &bars->abort_flag;
+
+  if (warp == 12) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      int issued = 0;
+      for (int t = 0; t < n; ++t) {
+        const int s = t % kStages;
+        if (!mbar_wait(&bars->st_empty[s], ((t / kStages) & 1) ^ 1, ctl)) break;
+        const int k0 = (tile0 + t) * kK;
+        mbar_expect_tx(&bars->st_full[s], Cfg::kABytes + Cfg::kBBytes);
+        tma_load_3d(smem + Cfg::a_hi(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
+#pragma unroll
+        for (int c = 0; c < N / 32; ++c)
+          tma_load_rows(smem + Cfg::b_hi(s) + c * kK * 128, &tm_b, c * 32, k0, hb, ob, &bars->st_full[s], HEADS);
+        issued = t + 1;
+      }
+      if (*ctl.abort_flag) {  // let the copies in flight land before the CTA exits
+        WaitCtl drain = ctl;
+        drain.deadline_ns = globaltimer_ns() + g.timeout_ns;
+        int dummy = 0;
+        drain.abort_flag = &dummy;
+        for (int t = (issued > kStages ? issued - kStages : 0); t < issued; ++t)
+          mbar_wait(&bars->st_full[t % kStages], (t / kStages) & 1, drain);
+      }
+    }
+  } else if (warp == 13) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && n > 0) {
+      const uint32_t sb = smem_u32(smem);
+      constexpr uint32_t idesc = make_idesc(128, N, false, true, true);
+      for (int t = 0; t < n; ++t) {
+        const int s = t % kStages, ab = t & 1;
+        // accumulator ab was folded by the epilogue (its use t - 2)
+        if (t >= 2 && !mbar_wait(&bars->acc_empty[ab], ((t >> 1) - 1) & 1, ctl)) break;
+        if (!mbar_wait(&bars->st_ready[s], (t / kStages) & 1, ctl)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + ab * N;
+#pragma unroll
+        for (int kk = 0; kk < kK / 8; ++kk) {
+          const uint64_t ah = make_sw128_desc(sb + Cfg::a_hi(s) + kk * 32, 16, 1024);
+          const uint64_t al = make_sw128_desc(sb + Cfg::a_lo(s) + kk * 32, 16, 1024);
+          const uint64_t bh = make_sw128_32b_desc(sb + Cfg::b_hi(s) + kk * 1024, kK * 128, 512);
+          const uint64_t bl = make_sw128_32b_desc(sb + Cfg::b_lo(s) + kk * 1024, kK * 128, 512);
+          mma_tf32_ss(acc, ah, bh, idesc, kk > 0 ? 1u : 0u);  // a fresh accumulator every tile
+          mma_tf32_ss(acc, ah, bl, idesc, 1u);
+          mma_tf32_ss(acc, al, bh, idesc, 1u);
+        }
+        mma_commit(&bars->st_empty[s]);
+        mma_commit(&bars->acc_full[ab]);
+      }
+      mma_commit(&bars->mma_done);
+      WaitCtl drain = ctl;
+      drain.deadline_ns = globaltimer_ns() + g.timeout_ns;
+      int dummy = 0;
+      drain.abort_flag = &dummy;
+      mbar_wait(&bars->mma_done, 0, drain);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------- converters
+    const int tid = threadIdx.x - 256;
+    for (int t = 0; t < n; ++t) {
+      const int s = t % kStages;
+      if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
+      split_tile(smem + Cfg::a_hi(s), smem + Cfg::a_lo(s), Cfg::kABytes, tid, 128);
+      split_tile(smem + Cfg::b_hi(s), smem + Cfg::b_lo(s), Cfg::kBBytes, tid, 128);
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->st_ready[s]);
+    }
+  } else {
+    // ---------------------------------------------------- epilogue warps
+    const int half = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float tot[kHC];
+#pragma unroll
+    for (int e = 0; e < kHC; ++e) tot[e] = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < n; ++t) {
+      const int ab = t & 1;
+      if (!tc::warp_wait(&bars->acc_full[ab], (t >> 1) & 1, ctl)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < (kHC + 31) / 32; ++c) {
+        constexpr int W = kHC < 32 ? kHC : 32;
+        uint32_t a[W];
+        gemm_tmem_ld<W>(tmem + lane_base + ab * N + half * kHC + c * 32, a);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < W; ++e) tot[c * 32 + e] += __uint_as_float(a[e]);
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[ab]);
+    }
+    const int64_t m = m0 + r;
+    if (ok && m < g.M) {
+      float* crow = g.c + row_offset_t<HEADS>(g.H, b, m, g.M, g.D);
+#pragma unroll
+      for (int q = 0; q < kHC / 4; ++q) {
+        const int col = half * kHC + 4 * q;
+        if (col < g.D)
+          *reinterpret_cast<float4*>(crow + col) = make_float4(tot[4 * q] * g.alpha, tot[4 * q + 1] * g.alpha,
+                                                               tot[4 * q + 2] * g.alpha, tot[4 * q + 3] * g.alpha);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// D_i = rowsum(dO_i * O_i) - dstats_i for every query row (the DQ pass computes
+// it in its prologue; the GEMM route has no DQ pass): one warp per row.
+template <bool HEADS>
+__global__ void __launch_bounds__(256) delta_kernel(const Params p) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= p.B * p.S_q) return;
+  const int64_t b = row / p.S_q, i = row - b * p.S_q;
+  const float* orow = static_cast<const float*>(p.o) + row_offset_t<HEADS>(p.H, b, i, p.S_q, p.D_v);
+  const float* grow = static_cast<const float*>(p.d_o) + row_offset_t<HEADS>(p.H, b, i, p.S_q, p.D_v);
+  float acc = 0.0f;
+  for (int c = 4 * lane; c < p.D_v; c += 128) {
+    const float4 o4 = *reinterpret_cast<const float4*>(orow + c);
+    const float4 g4 = *reinterpret_cast<const float4*>(grow + c);
+    acc = fmaf(g4.x, o4.x, acc);
+    acc = fmaf(g4.y, o4.y, acc);
+    acc = fmaf(g4.z, o4.z, acc);
+    acc = fmaf(g4.w, o4.w, acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) p.delta[row] = p.d_stats ? acc - p.d_stats[row] : acc;
+}
+
+}  // namespace tf32
+}  // namespace sdpa_b200

@@ -3,6 +3,7 @@
 #include "ptx.cuh"
 #include "tf32_bwd.cuh"
 #include "tf32_fwd.cuh"
+#include "tf32_gemm.cuh"
 
 using namespace sdpa_b200;
 using namespace sdpa_b200::host;
@@ -35,11 +36,11 @@ int launch_fwd_d(const Params& p, cudaStream_t st, int* launches) {
                       : launch_fwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
-template <int MODE, int DQK, int DV, bool DROP, bool HEADS>
+template <int MODE, int DQK, int DV, bool DROP, bool HEADS, bool WS = false>
 int launch_bwd_mode(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tf32::BwdCfg<MODE, DQK, DV>;
-  auto kern = tf32::bwd_kernel<MODE, DQK, DV, DROP, HEADS>;
+  auto kern = tf32::bwd_kernel<MODE, DQK, DV, DROP, HEADS, WS>;
   if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
   const bool rows_q = MODE == tf32::kDQ;
   CUtensorMap ma, mb;
@@ -69,8 +70,67 @@ int launch_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   return SDPA_B200_OK;
 }
 
+// C = alpha * A B over the materialised matrix A ([B, M, ld], row length K)
+// and the [B/H, K, H, N] operand b_src.
+template <int N, bool HEADS>
+int launch_gemm(const float* a, int64_t ld, const void* b_src, int d_b, float* c, const Params& p, int64_t M,
+                int64_t K, float alpha, int range, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tf32::GemmCfg<N>;
+  auto kern = tf32::gemm_kernel<N, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
+  CUtensorMap ma, mb;
+  if (!make_map_rows_f32(&ma, a, p.B, M, K, ld, 128) || !make_map_f32_mn(&mb, b_src, p.B, p.H, K, d_b, Cfg::kK))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map
+  tf32::GemmArgs g;
+  g.c = c;
+  g.B = p.B;
+  g.H = p.H;
+  g.M = M;
+  g.K = K;
+  g.D = d_b;
+  g.alpha = alpha;
+  g.range = range;
+  g.timeout_ns = p.timeout_ns;
+  const int64_t grid = ((M + 127) / 128) * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tf32::kGemmThreads, Cfg::kSmemBytes, st>>>(ma, mb, g);
+  ++*launches;
+  return launch_result();
+}
+
+// The GEMM route (p.ws_ds / p.ws_p set): D, then the DK pass writing dS and
+// P~^T, then dQ = scale dS K and dV = P~^T dO as GEMMs.
+template <int DQK, int DV, bool DROP, bool HEADS>
+int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
+  sdpa_b200::record_bwd_event(0, st);
+  const int64_t rows = p.B * p.S_q;
+  tf32::delta_kernel<HEADS><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
+  ++*launches;
+  if (int r = launch_result()) return r;
+  if (int r = launch_bwd_mode<tf32::kDK, DQK, DV, DROP, HEADS, true>(p, st, launches)) return r;
+  sdpa_b200::record_bwd_event(1, st);
+  const int range_q = p.causal ? 1 : 0, range_v = p.causal ? 2 : 0;
+  if (int r = launch_gemm<DQK, HEADS>(p.ws_ds, p.ld_ds, p.k, p.D_qk, static_cast<float*>(p.dq), p, p.S_q, p.S_kv,
+                                      p.scale, range_q, st, launches))
+    return r;
+  sdpa_b200::record_bwd_event(2, st);
+  if (int r = launch_gemm<DV, HEADS>(p.ws_p, p.ld_p, p.d_o, p.D_v, static_cast<float*>(p.dv), p, p.S_kv, p.S_q,
+                                     1.0f, range_v, st, launches))
+    return r;
+  sdpa_b200::record_bwd_event(3, st);
+  return SDPA_B200_OK;
+}
+
 template <int DQK, int DV>
 int launch_bwd_d(const Params& p, cudaStream_t st, int* launches) {
+  if (p.ws_ds) {
+    if (p.H > 1)
+      return p.dropout_on ? launch_bwd_gemm_t<DQK, DV, true, true>(p, st, launches)
+                          : launch_bwd_gemm_t<DQK, DV, false, true>(p, st, launches);
+    return p.dropout_on ? launch_bwd_gemm_t<DQK, DV, true, false>(p, st, launches)
+                        : launch_bwd_gemm_t<DQK, DV, false, false>(p, st, launches);
+  }
   if (p.H > 1)
     return p.dropout_on ? launch_bwd_t<DQK, DV, true, true>(p, st, launches)
                         : launch_bwd_t<DQK, DV, false, true>(p, st, launches);
