@@ -277,13 +277,14 @@ def run_ours(args, w):
     path = fa.kernel_path(dt, Dq, Dv, backward=True)
     # per-kernel timing of the backward on the launching stream, through the
     # library's diagnostic event hook: fp16 runs dQ then dK/dV; fp32 either the
-    # GEMM route (D + the DK pass writing dS and P~^T, then the dQ and dV GEMMs,
-    # when the workspace query asks for room for them) or the passes dQ, dK, dV
+    # GEMM route (D + the score pass writing dS and P~^T, then the dQ, dK and dV
+    # GEMMs, when the workspace query asks for room for them) or the passes dQ, dK, dV
     tf32_gemm = (dt == torch.float32 and fa._lib.lib().sdpa_b200_bwd_workspace_bytes(
         fa._lib.F32, B, S, S_kv, Dq, Dv) > B * S * 4)
     knames = {"tcgen05": ("dq2_kernel", "dkdv_kernel"),
-              "tcgen05-3xtf32": (("tf32 D + dK pass", "tf32 dQ gemm", "tf32 dV gemm") if tf32_gemm
+              "tcgen05-3xtf32": (("tf32 D + score pass", "tf32 dQ gemm", "tf32 dK gemm", "tf32 dV gemm") if tf32_gemm
                                  else ("tf32 dQ", "tf32 dK", "tf32 dV"))}.get(path)
+    n_ev = 5 if knames and len(knames) == 4 else 4
     launches = [0]
     kev = []
     last = {}
@@ -294,11 +295,11 @@ def run_ours(args, w):
         e_mid = torch.cuda.Event(enable_timing=True)
         e_mid.record(stream)
         if knames and record:
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
             for e in evs:  # torch creates the CUDA event on its first record
                 e.record(stream)
-            arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
-            fa._lib.lib().sdpa_b200_set_bwd_events(arr, 4)
+            arr = (ctypes.c_void_p * n_ev)(*[e.cuda_event for e in evs])
+            fa._lib.lib().sdpa_b200_set_bwd_events(arr, n_ev)
             kev.append(evs)
         dq, dk, dv = fa.sdpa_grad(q, k, v, o, s, do, w["seed"], off, **kw)
         if knames and record:
@@ -478,9 +479,9 @@ def run_ours(args, w):
     if kernel_ms and path == "tcgen05":
         cands += [("dkdv_kernel", kernel_ms["dkdv_kernel"], unit * (2 * Dq + 2 * Dv)),
                   ("dq2_kernel", kernel_ms["dq2_kernel"], unit * Dq)]
-    elif kernel_ms:  # fp32: the dK pass carries S, dP, dK; dQ and dV one product each, on either route
+    elif kernel_ms:  # fp32 passes: the dK pass carries S, dP, dK; GEMM route: the score pass S, dP
         share = {"tf32 dQ": Dq, "tf32 dK": 2 * Dq + Dv, "tf32 dV": Dv,
-                 "tf32 D + dK pass": 2 * Dq + Dv, "tf32 dQ gemm": Dq, "tf32 dV gemm": Dv}
+                 "tf32 D + score pass": Dq + Dv, "tf32 dQ gemm": Dq, "tf32 dK gemm": Dq, "tf32 dV gemm": Dv}
         cands += [(n, kernel_ms[n], unit * share[n]) for n in knames]
     else:
         cands += [("bwd (all kernels)", bwd_ms, mf_bwd)]

@@ -55,14 +55,19 @@ int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* 
                   int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, float scale, float dropout, int causal,
                   uint64_t seed, uint64_t offset, void* stream);
 
-/* Scratch the backward needs: one float32 per query row (rowsum(dO*O)).
- * The caller allocates it (TF: allocate_temp). */
+/* Scratch the backward asks for (the caller allocates it; TF: allocate_temp):
+ * one float32 per query row (rowsum(dO*O)), which is also the minimum
+ * sdpa_b200_bwd accepts; for fp32 shapes on the tensor-core path (D_qk <= 64)
+ * also room for dS and (dropout-scaled P)^T, about 4*B*S_q*S_kv bytes each,
+ * up to 4 GiB in all, which selects the faster GEMM route of the backward. */
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v);
 
 /* Backward: dq, dk, dv shaped like q, k, v (dtype), from q, k, v, out, stats
  * and d_out of the forward, no atomics: fp16 runs two kernels, dQ (which
- * also writes rowsum(dO*O) to the workspace) then dK/dV; fp32 runs three
- * (dQ, dK, dV) on the 3xTF32 tensor-core path.
+ * also writes rowsum(dO*O) to the workspace) then dK/dV; fp32 runs on the
+ * 3xTF32 tensor-core path, with the full workspace as five kernels (rowsum,
+ * a score pass writing dS and P~^T, then dQ, dK and dV as GEMMs), with the
+ * minimum as three recomputing passes (dQ, dK, dV).
  * Replaces FlashAttnGradFunctor<GPUDevice,T> (sdpa/sdpa_bwd.cu.cc:347-453). */
 int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
                   const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,
@@ -156,10 +161,13 @@ int sdpa_b200_bwd_noalloc(int dtype, const void* q, const void* k, const void* v
                           int causal, uint64_t seed, uint64_t offset, void* stream);
 
 /* Diagnostic: when events != NULL, the next tensor-core backward calls on
- * this host thread record events[0..3] (cudaEvent_t) on their stream before
- * the dQ kernel (which also computes the rowsum D), before the dK/dV kernel,
- * and after it (events[2] and [3] both), so a caller can time each kernel.
- * n must be 4; NULL turns it off. */
+ * this host thread record events[0..n-1] (cudaEvent_t, 4 <= n <= 8) on their
+ * stream between their launches, so a caller can time each kernel:
+ *   fp16: [0] dQ (+ rowsum D) [1] dK/dV [2], [3] = [2];
+ *   fp32 passes: [0] dQ [1] dK [2] dV [3];
+ *   fp32 GEMM route: [0] D + score pass [1] dQ GEMM [2] dK GEMM [3] dV GEMM [4]
+ *   (with n = 4 the last interval is not recorded).
+ * NULL turns it off. */
 int sdpa_b200_set_bwd_events(void* const* events, int n);
 
 /* ABI version (major*100 + minor). */

@@ -23,7 +23,7 @@ namespace {
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
 std::atomic<uint64_t> g_timeout_ns{kDefaultTimeoutNs};
 thread_local int t_launches = 0;
-thread_local void* t_bwd_event_store[4];  // copy of the caller's events
+thread_local void* t_bwd_event_store[8];  // copy of the caller's events
 
 // The TMA descriptors are encoded through the driver API, which needs a
 // current context on the calling thread.  A thread that has made no runtime
@@ -361,8 +361,8 @@ int sdpa_b200_set_bwd_events(void* const* events, int n) {
     t_bwd_events = nullptr;
     return SDPA_B200_OK;
   }
-  if (n != 4) return SDPA_B200_EINVAL;
-  for (int i = 0; i < 4; ++i) t_bwd_event_store[i] = events[i];
+  if (n < 4 || n > 8) return SDPA_B200_EINVAL;
+  for (int i = 0; i < 8; ++i) t_bwd_event_store[i] = i < n ? events[i] : nullptr;
   t_bwd_events = t_bwd_event_store;
   return SDPA_B200_OK;
 }

@@ -99,10 +99,11 @@ inline bool make_map_f32_mn(CUtensorMap* m, const void* base, int64_t B, int64_t
 }
 
 // fp32 matrices [B, M, ld] (row length K <= ld, ld a multiple of 4) as the
-// 3-D map (column, row, batch), box 32 columns x `rows` rows, 128B swizzle;
-// columns beyond K and rows beyond M read as zero.
+// 3-D map (column, row, batch), box 32 columns x `rows` rows, 128B swizzle
+// (or its 32-byte-atom form for MN-major reads); columns beyond K and rows
+// beyond M read as zero.
 inline bool make_map_rows_f32(CUtensorMap* m, const float* base, int64_t B, int64_t M, int64_t K, int64_t ld,
-                              int rows) {
+                              int rows, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return map_failure(0, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(B)};
@@ -110,7 +111,7 @@ inline bool make_map_rows_f32(CUtensorMap* m, const float* base, int64_t B, int6
   cuuint32_t box[3] = {32, static_cast<cuuint32_t>(rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS || map_failure(static_cast<int>(r), "cuTensorMapEncodeTiled");
 }
@@ -138,7 +139,7 @@ inline int launch_result() {
 // Optional events recorded between the backward's launches (diagnostic).
 extern thread_local void* const* t_bwd_events;
 inline void record_bwd_event(int i, cudaStream_t st) {
-  if (t_bwd_events) cudaEventRecord(static_cast<cudaEvent_t>(t_bwd_events[i]), st);
+  if (t_bwd_events && i < 8 && t_bwd_events[i]) cudaEventRecord(static_cast<cudaEvent_t>(t_bwd_events[i]), st);
 }
 
 // Launchers, one per translation unit (launch count added to *launches).

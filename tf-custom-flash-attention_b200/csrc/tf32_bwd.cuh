@@ -172,9 +172,7 @@ __device__ __forceinline__ void issue_scores(uint32_t out, uint32_t ah, uint32_t
   }
 }
 
-// WS (DK only): also write dS and P~^T to the workspace for the GEMM route
-// (tf32_gemm.cuh), which then replaces the DQ and DV passes.
-template <int MODE, int DQK, int DV, bool DROP, bool HEADS, bool WS = false>
+template <int MODE, int DQK, int DV, bool DROP, bool HEADS>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_sa, const __grid_constant__ CUtensorMap tm_sb, const Params p) {
   using Cfg = BwdCfg<MODE, DQK, DV>;
@@ -495,12 +493,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         LcgWalk st(DROP ? lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + c0g) * static_cast<uint64_t>(p.S_kv),
                                     static_cast<uint64_t>(rr))
                         : 0);
-        static_assert(!WS || MODE == kDK, "only the DK pass materialises");
-        // WS: P~^T row rr, columns c0g.. (ld_p covers every streamed column), and
-        // dS column rr of query rows c0g.. (consecutive lanes, consecutive keys)
-        float* const p_row = WS ? p.ws_p + (b * p.S_kv + rr) * p.ld_p + c0g : nullptr;
-        float* const ds_col = WS ? p.ws_ds + (b * p.S_q + c0g) * p.ld_ds + rr : nullptr;
-        float pk4[4];
 #pragma unroll
         for (int c = 0; c < kHalf; ++c) {
           float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -vec[c]));
@@ -511,13 +503,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             st.step(step_lo, step_hi);
           }
           const float x = MODE == kDK ? pr * fmaf(kf, __uint_as_float(dpv[c]), -vec[kN + c]) : pr * kf;
-          if constexpr (WS) {
-            pk4[c & 3] = pr * kf;
-            if (row_ok) {
-              if ((c & 3) == 3) *reinterpret_cast<float4*>(p_row + c - 3) = make_float4(pk4[0], pk4[1], pk4[2], pk4[3]);
-              if (c0g + c < p.S_q) ds_col[static_cast<int64_t>(c) * p.ld_ds] = x;
-            }
-          }
           float h, w;
           split_tf32(x, h, w);
           hv[c] = __float_as_uint(h);

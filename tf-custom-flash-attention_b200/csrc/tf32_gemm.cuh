@@ -1,15 +1,17 @@
-// fp32 backward, second stage: dQ and dV as plain 3xTF32 GEMMs over the
-// score-shaped gradients the DK pass materialised (tf32_bwd.cuh, WS = true):
+// fp32 backward, second stage of the GEMM route: dQ, dK and dV as plain
+// 3xTF32 GEMMs over the score-shaped gradients the score pass materialised
+// (tf32_scores.cuh):
 //
-//   dQ[b] = scale * dS[b] K[b]        M = S_q rows, K-dim = S_kv
+//   dQ[b] = scale * dS[b] K[b]        M = S_q rows,  K-dim = S_kv
+//   dK[b] = scale * dS[b]^T Q[b]      M = S_kv rows, K-dim = S_q (dS read MN-major)
 //   dV[b] =         P~^T[b] dO[b]     M = S_kv rows, K-dim = S_q
 //
 // with dS = P (kf dP - D) and P~ = kf P, exactly the matrices the reference's
 // dQ and dK/dV kernels form element by element (sdpa/sdpa_bwd.cu.cc:125-170).
-// Recomputing them per pass (S, dP for dQ; S for dV) costs the fp32 path more
-// tensor time than reading them back: every recomputed product is three tf32
-// MMAs, and with hi / lo operands resident the recomputing passes only fit
-// N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
+// Recomputing them per pass (S, dP for dQ and dK; S for dV) costs the fp32
+// path more tensor time than reading them back: every recomputed product is
+// three tf32 MMAs, and with hi / lo operands resident the recomputing passes
+// only fit N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
 //
 // One CTA = 128 rows of the result, all N columns.  Streams K-dim tiles of 32:
 // the A tile (128 x 32, K-major, 128-byte swizzle) and the B tile (32 x N,
@@ -17,8 +19,9 @@
 // four converter warps; one thread issues 4 x 3 SS MMAs per tile into one of
 // two TMEM accumulators, which 8 epilogue warps fold into an fp32 running
 // total every tile (the tensor cores' accumulation is not round-to-nearest).
-// Causal ranges: dQ row tile m0 needs keys < m0 + 128, dV row tile m0 queries
-// >= m0; every entry inside those ranges was written (masked ones as zero).
+// Causal ranges: dQ row tile m0 needs keys < m0 + 128, dK / dV row tile m0
+// queries >= m0; every entry inside those ranges was written (masked ones as
+// zero).
 #pragma once
 #include "common.cuh"
 #include "fwd_tc.cuh"
@@ -30,12 +33,24 @@ namespace tf32 {
 
 constexpr int kGemmThreads = 448;
 
+// Timing probe for tuning builds (-DSDPA_B200_TF32_PROBE=3
+// -DSDPA_B200_GEMM_PROBE_N=<N>): SM cycles of CTA 0's roles, as in the passes.
+#if defined(SDPA_B200_TF32_PROBE) && defined(SDPA_B200_GEMM_PROBE_N)
+#define GEMM_PROBE_T0(v) const long long v = clock64()
+#define GEMM_PROBE_ADD(slot, t0)                                      \
+  if (blockIdx.x == 0 && N == SDPA_B200_GEMM_PROBE_N) \
+  atomicAdd(&g_tf32_probe[slot], static_cast<unsigned long long>(clock64() - (t0)))
+#else
+#define GEMM_PROBE_T0(v)
+#define GEMM_PROBE_ADD(slot, t0)
+#endif
+
 struct GemmArgs {
   float* c;          // result [B/H, M, H, D] (H = 1: [B, M, D])
   int64_t B, H, M, K;
   int D;             // result columns (<= N)
   float alpha;
-  int range;         // 0: whole K-dim, 1: K-dim < m0 + 128 (dQ, causal), 2: K-dim >= m0 (dV, causal)
+  int range;         // 0: whole K-dim, 1: K-dim < m0 + 128 (dQ, causal), 2: K-dim >= m0 (dK, dV, causal)
   uint64_t timeout_ns;
 };
 
@@ -75,9 +90,12 @@ __device__ __forceinline__ void gemm_tmem_ld(uint32_t taddr, uint32_t* r) {
   }
 }
 
-// tm_a: 3-D map (K-dim, row, batch) of the materialised matrix, box 32 x 128.
-// tm_b: MN-major map (32-byte atoms) of K or dO, box 32 columns x 32 rows.
-template <int N, bool HEADS>
+// tm_a: 3-D map of the materialised matrix: K-major (A_MN false: K-dim
+// innermost, box 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN true: the
+// stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
+// atoms; dK reads dS this way).  tm_b: MN-major map of K, Q or dO, box 32
+// columns x 32 K-dim.
+template <int N, bool HEADS, bool A_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
   using Cfg = GemmCfg<N>;
@@ -91,7 +109,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int64_t b, tord;
   raster(blockIdx.x, g.B, n_mt, b, tord);
   const int hb = HEADS ? static_cast<int>(b % g.H) : 0, ob = HEADS ? static_cast<int>(b / g.H) : static_cast<int>(b);
-  // heaviest causal row tiles first: high ones for dQ, low ones for dV
+  // heaviest causal row tiles first: high ones for dQ, low ones for dK / dV
   const int64_t m0 = (g.range == 1 ? n_mt - 1 - tord : tord) * 128;
   const int64_t n_all = (g.K + kK - 1) / kK;
   int tile0 = 0, n = static_cast<int>(n_all);
@@ -133,10 +151,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int issued = 0;
       for (int t = 0; t < n; ++t) {
         const int s = t % kStages;
+        GEMM_PROBE_T0(p0);
         if (!mbar_wait(&bars->st_empty[s], ((t / kStages) & 1) ^ 1, ctl)) break;
+        GEMM_PROBE_ADD(8, p0);
         const int k0 = (tile0 + t) * kK;
         mbar_expect_tx(&bars->st_full[s], Cfg::kABytes + Cfg::kBBytes);
-        tma_load_3d(smem + Cfg::a_hi(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
+        if (A_MN) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tma_load_3d(smem + Cfg::a_hi(s) + c * kK * 128, &tm_a, static_cast<int>(m0) + c * 32, k0,
+                        static_cast<int>(b), &bars->st_full[s]);
+        } else {
+          tma_load_3d(smem + Cfg::a_hi(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
+        }
 #pragma unroll
         for (int c = 0; c < N / 32; ++c)
           tma_load_rows(smem + Cfg::b_hi(s) + c * kK * 128, &tm_b, c * 32, k0, hb, ob, &bars->st_full[s], HEADS);
@@ -155,18 +182,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------- MMA issuer
     if (lane == 0 && n > 0) {
       const uint32_t sb = smem_u32(smem);
-      constexpr uint32_t idesc = make_idesc(128, N, false, true, true);
+      constexpr uint32_t idesc = make_idesc(128, N, A_MN, true, true);
       for (int t = 0; t < n; ++t) {
         const int s = t % kStages, ab = t & 1;
         // accumulator ab was folded by the epilogue (its use t - 2)
+        GEMM_PROBE_T0(w0);
         if (t >= 2 && !mbar_wait(&bars->acc_empty[ab], ((t >> 1) - 1) & 1, ctl)) break;
+        GEMM_PROBE_ADD(0, w0);
+        GEMM_PROBE_T0(w1);
         if (!mbar_wait(&bars->st_ready[s], (t / kStages) & 1, ctl)) break;
+        GEMM_PROBE_ADD(1, w1);
+        GEMM_PROBE_T0(w2);
         tc_fence_after();
         const uint32_t acc = tmem + ab * N;
 #pragma unroll
         for (int kk = 0; kk < kK / 8; ++kk) {
-          const uint64_t ah = make_sw128_desc(sb + Cfg::a_hi(s) + kk * 32, 16, 1024);
-          const uint64_t al = make_sw128_desc(sb + Cfg::a_lo(s) + kk * 32, 16, 1024);
+          const uint64_t ah = A_MN ? make_sw128_32b_desc(sb + Cfg::a_hi(s) + kk * 1024, kK * 128, 512)
+                                   : make_sw128_desc(sb + Cfg::a_hi(s) + kk * 32, 16, 1024);
+          const uint64_t al = A_MN ? make_sw128_32b_desc(sb + Cfg::a_lo(s) + kk * 1024, kK * 128, 512)
+                                   : make_sw128_desc(sb + Cfg::a_lo(s) + kk * 32, 16, 1024);
           const uint64_t bh = make_sw128_32b_desc(sb + Cfg::b_hi(s) + kk * 1024, kK * 128, 512);
           const uint64_t bl = make_sw128_32b_desc(sb + Cfg::b_lo(s) + kk * 1024, kK * 128, 512);
           mma_tf32_ss(acc, ah, bh, idesc, kk > 0 ? 1u : 0u);  // a fresh accumulator every tile
@@ -175,6 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         mma_commit(&bars->st_empty[s]);
         mma_commit(&bars->acc_full[ab]);
+        GEMM_PROBE_ADD(2, w2);
       }
       mma_commit(&bars->mma_done);
       WaitCtl drain = ctl;
@@ -188,10 +223,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int tid = threadIdx.x - 256;
     for (int t = 0; t < n; ++t) {
       const int s = t % kStages;
+      GEMM_PROBE_T0(c0);
       if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
+      if (tid == 0) GEMM_PROBE_ADD(6, c0);
+      GEMM_PROBE_T0(c1);
       split_tile(smem + Cfg::a_hi(s), smem + Cfg::a_lo(s), Cfg::kABytes, tid, 128);
       split_tile(smem + Cfg::b_hi(s), smem + Cfg::b_lo(s), Cfg::kBBytes, tid, 128);
       fence_proxy_async_smem();
+      if (tid == 0) GEMM_PROBE_ADD(7, c1);
       mbar_arrive(&bars->st_ready[s]);
     }
   } else {
@@ -205,10 +244,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     bool ok = true;
     for (int t = 0; t < n; ++t) {
       const int ab = t & 1;
+      GEMM_PROBE_T0(e0);
       if (!tc::warp_wait(&bars->acc_full[ab], (t >> 1) & 1, ctl)) {
         ok = false;
         break;
       }
+      if (threadIdx.x == 0) GEMM_PROBE_ADD(4, e0);
+      GEMM_PROBE_T0(e1);
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < (kHC + 31) / 32; ++c) {
@@ -220,6 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int e = 0; e < W; ++e) tot[c * 32 + e] += __uint_as_float(a[e]);
       }
       tc_fence_before();
+      if (threadIdx.x == 0) GEMM_PROBE_ADD(5, e1);
       mbar_arrive(&bars->acc_empty[ab]);
     }
     const int64_t m = m0 + r;
@@ -243,8 +286,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// D_i = rowsum(dO_i * O_i) - dstats_i for every query row (the DQ pass computes
-// it in its prologue; the GEMM route has no DQ pass): one warp per row.
+// D_i = rowsum(dO_i * O_i) - dstats_i for every query row (the DQ pass of the
+// recomputing route computes it in its prologue): one warp per row.
 template <bool HEADS>
 __global__ void __launch_bounds__(256) delta_kernel(const Params p) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;

@@ -4,6 +4,7 @@
 #include "tf32_bwd.cuh"
 #include "tf32_fwd.cuh"
 #include "tf32_gemm.cuh"
+#include "tf32_scores.cuh"
 
 using namespace sdpa_b200;
 using namespace sdpa_b200::host;
@@ -36,11 +37,11 @@ int launch_fwd_d(const Params& p, cudaStream_t st, int* launches) {
                       : launch_fwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
-template <int MODE, int DQK, int DV, bool DROP, bool HEADS, bool WS = false>
+template <int MODE, int DQK, int DV, bool DROP, bool HEADS>
 int launch_bwd_mode(const Params& p, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tf32::BwdCfg<MODE, DQK, DV>;
-  auto kern = tf32::bwd_kernel<MODE, DQK, DV, DROP, HEADS, WS>;
+  auto kern = tf32::bwd_kernel<MODE, DQK, DV, DROP, HEADS>;
   if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
   const bool rows_q = MODE == tf32::kDQ;
   CUtensorMap ma, mb;
@@ -70,17 +71,19 @@ int launch_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   return SDPA_B200_OK;
 }
 
-// C = alpha * A B over the materialised matrix A ([B, M, ld], row length K)
-// and the [B/H, K, H, N] operand b_src.
-template <int N, bool HEADS>
+// C = alpha * A B over the materialised matrix a ([B, rows, ld]; A itself,
+// or with A_MN its transpose) and the [B/H, K, H, N] operand b_src.
+template <int N, bool HEADS, bool A_MN>
 int launch_gemm(const float* a, int64_t ld, const void* b_src, int d_b, float* c, const Params& p, int64_t M,
                 int64_t K, float alpha, int range, cudaStream_t st, int* launches) {
   static std::atomic<uint64_t> attr_done{0};
   using Cfg = tf32::GemmCfg<N>;
-  auto kern = tf32::gemm_kernel<N, HEADS>;
+  auto kern = tf32::gemm_kernel<N, HEADS, A_MN>;
   if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
   CUtensorMap ma, mb;
-  if (!make_map_rows_f32(&ma, a, p.B, M, K, ld, 128) || !make_map_f32_mn(&mb, b_src, p.B, p.H, K, d_b, Cfg::kK))
+  const bool ok_a = A_MN ? make_map_rows_f32(&ma, a, p.B, K, M, ld, Cfg::kK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                         : make_map_rows_f32(&ma, a, p.B, M, K, ld, 128);
+  if (!ok_a || !make_map_f32_mn(&mb, b_src, p.B, p.H, K, d_b, Cfg::kK))
     return SDPA_B200_ECUDA;  // detail recorded by make_map
   tf32::GemmArgs g;
   g.c = c;
@@ -99,8 +102,25 @@ int launch_gemm(const float* a, int64_t ld, const void* b_src, int d_b, float* c
   return launch_result();
 }
 
-// The GEMM route (p.ws_ds / p.ws_p set): D, then the DK pass writing dS and
-// P~^T, then dQ = scale dS K and dV = P~^T dO as GEMMs.
+template <int DQK, int DV, bool DROP, bool HEADS>
+int launch_scores(const Params& p, cudaStream_t st, int* launches) {
+  static std::atomic<uint64_t> attr_done{0};
+  using Cfg = tf32::ScoreCfg<DQK, DV>;
+  auto kern = tf32::score_kernel<DQK, DV, DROP, HEADS>;
+  if (cudaError_t e = ensure_smem(kern, Cfg::kSmemBytes, attr_done)) return cuda_failure("shared-memory attribute", e);
+  CUtensorMap mq, mo;
+  if (!make_map_f32(&mq, p.q, p.B, p.H, p.S_q, p.D_qk, Cfg::kN) ||
+      !make_map_f32(&mo, p.d_o, p.B, p.H, p.S_q, p.D_v, Cfg::kN))
+    return SDPA_B200_ECUDA;  // detail recorded by make_map
+  const int64_t grid = ((p.S_kv + 127) / 128) * p.B;
+  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  kern<<<static_cast<unsigned>(grid), tf32::kScoreThreads, Cfg::kSmemBytes, st>>>(mq, mo, p);
+  ++*launches;
+  return launch_result();
+}
+
+// The GEMM route (p.ws_ds / p.ws_p set): D, the score pass writing dS and
+// P~^T, then dQ = scale dS K, dK = scale dS^T Q and dV = P~^T dO as GEMMs.
 template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
   sdpa_b200::record_bwd_event(0, st);
@@ -108,17 +128,21 @@ int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
   tf32::delta_kernel<HEADS><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
   ++*launches;
   if (int r = launch_result()) return r;
-  if (int r = launch_bwd_mode<tf32::kDK, DQK, DV, DROP, HEADS, true>(p, st, launches)) return r;
+  if (int r = launch_scores<DQK, DV, DROP, HEADS>(p, st, launches)) return r;
   sdpa_b200::record_bwd_event(1, st);
-  const int range_q = p.causal ? 1 : 0, range_v = p.causal ? 2 : 0;
-  if (int r = launch_gemm<DQK, HEADS>(p.ws_ds, p.ld_ds, p.k, p.D_qk, static_cast<float*>(p.dq), p, p.S_q, p.S_kv,
-                                      p.scale, range_q, st, launches))
+  const int range_q = p.causal ? 1 : 0, range_kv = p.causal ? 2 : 0;
+  if (int r = launch_gemm<DQK, HEADS, false>(p.ws_ds, p.ld_ds, p.k, p.D_qk, static_cast<float*>(p.dq), p, p.S_q,
+                                             p.S_kv, p.scale, range_q, st, launches))
     return r;
   sdpa_b200::record_bwd_event(2, st);
-  if (int r = launch_gemm<DV, HEADS>(p.ws_p, p.ld_p, p.d_o, p.D_v, static_cast<float*>(p.dv), p, p.S_kv, p.S_q,
-                                     1.0f, range_v, st, launches))
+  if (int r = launch_gemm<DQK, HEADS, true>(p.ws_ds, p.ld_ds, p.q, p.D_qk, static_cast<float*>(p.dk), p, p.S_kv,
+                                            p.S_q, p.scale, range_kv, st, launches))
     return r;
   sdpa_b200::record_bwd_event(3, st);
+  if (int r = launch_gemm<DV, HEADS, false>(p.ws_p, p.ld_p, p.d_o, p.D_v, static_cast<float*>(p.dv), p, p.S_kv,
+                                            p.S_q, 1.0f, range_kv, st, launches))
+    return r;
+  sdpa_b200::record_bwd_event(4, st);
   return SDPA_B200_OK;
 }
 
