@@ -66,8 +66,8 @@ size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t 
  * and d_out of the forward, no atomics: fp16 runs two kernels, dQ (which
  * also writes rowsum(dO*O) to the workspace) then dK/dV; fp32 runs on the
  * 3xTF32 tensor-core path, with the full workspace as five kernels (rowsum,
- * a score pass writing dS and P~^T, then dQ, dK and dV as GEMMs), with the
- * minimum as three recomputing passes (dQ, dK, dV).
+ * a score pass writing dS and the dropout-scaled P, then dQ, dK and dV as
+ * GEMMs), with the minimum as three recomputing passes (dQ, dK, dV).
  * Replaces FlashAttnGradFunctor<GPUDevice,T> (sdpa/sdpa_bwd.cu.cc:347-453). */
 int sdpa_b200_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const float* stats,
                   const void* d_out, void* dq, void* dk, void* dv, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk,

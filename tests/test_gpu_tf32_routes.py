@@ -2,8 +2,8 @@
 (needs a B200).
 
 * GEMM route (the workspace sdpa_b200_bwd_workspace_bytes asks for): D, the
-  score pass writing dS and P~^T, then dQ = scale dS K, dK = scale dS^T Q and
-  dV = P~^T dO as GEMMs (5 launches).
+  score pass writing dS and P~ (dropout-scaled P), then dQ = scale dS K,
+  dK = scale dS^T Q and dV = P~^T dO as GEMMs (5 launches).
 * Recomputing route (a workspace of one float per query row, as the
   reference's op allocates): DQ, DK and DV passes (3 launches).
 
@@ -75,12 +75,12 @@ def test_both_routes_match_oracle(B, S_q, S_kv, D_qk, D_v, causal, p):
 
 
 def test_workspace_query_sizes_the_gemm_route():
-    """fp32 shapes the route serves ask for dS and P~^T; fp16 and shapes over
+    """fp32 shapes the route serves ask for dS and P~; fp16 and shapes over
     the cap ask for one float per query row."""
     L = fa._lib.lib()
     B, S_q, S_kv = 2, 100, 70
     full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 64, 128)
-    assert full >= B * S_q * 4 + B * S_q * 72 * 4 + B * S_kv * 128 * 4
+    assert full >= B * S_q * 4 + 2 * B * S_q * 72 * 4  # dS, P~: rows of S_kv padded to 16 bytes
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F16, B, S_q, S_kv, 64, 128) == B * S_q * 4
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) == B * S_q * 4
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4

@@ -13,7 +13,7 @@ LIB = os.path.join(HERE, "libsdpa_b200.so")
 SOURCES = [os.path.join(HERE, "csrc", f) for f in ("simt_bwd_f32.cu", "simt_bwd_f16.cu", "simt_fwd_f32.cu", "simt_fwd_f16.cu",
                                                    "bwd_tc.cu", "fwd_tc.cu", "tf32_tc.cu", "api.cu")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in ("common.cuh", "ptx.cuh", "simt.cuh", "fwd_tc.cuh",
-                                                          "bwd_tc.cuh", "tf32_fwd.cuh", "tf32_bwd.cuh", "tf32_gemm.cuh", "host.cuh", "simt_launch.cuh")] + [
+                                                          "bwd_tc.cuh", "tf32_fwd.cuh", "tf32_bwd.cuh", "tf32_gemm.cuh", "tf32_scores.cuh", "host.cuh", "simt_launch.cuh")] + [
     os.path.join(os.path.dirname(HERE), "include", "sdpa_b200.h")]
 NVCC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
 FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",

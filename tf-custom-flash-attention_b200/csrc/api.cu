@@ -202,9 +202,9 @@ int sdpa_b200_fwd_bshd(int dtype, const void* q, const void* k, const void* v, v
                   stream);
 }
 
-// Workspace of the fp32 backward's GEMM route beyond the delta rows: dS
-// [B, S_q, ld_ds] and P~^T [B, S_kv, ld_p] (ld_p covers every column the DK
-// pass's tiles write), or 0 where the route does not apply.  Capped so that
+// Workspace of the fp32 backward's GEMM route beyond the delta rows: dS and
+// P~, [B, S_q, ld_k] each (ld_k = S_kv rounded up to 16 bytes), or 0 where
+// the route does not apply.  Capped so that
 // the workspace stays a small part of HBM; above the cap (and with a smaller
 // workspace) the three recomputing passes run instead.
 constexpr size_t kGemmWorkspaceCap = size_t(4) << 30;
@@ -215,9 +215,8 @@ static size_t delta_bytes(int64_t B, int64_t S_q) {
 static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
   if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
   if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return 0;
-  const size_t ds = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
-  const size_t pt = static_cast<size_t>(round_up(B * S_kv * round_up(S_q, 64) * 4, 256));
-  return ds + pt <= kGemmWorkspaceCap ? ds + pt : 0;
+  const size_t one = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
+  return 2 * one <= kGemmWorkspaceCap ? 2 * one : 0;
 }
 
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
@@ -261,10 +260,9 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
     const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
     if (extra && workspace_bytes >= delta_bytes(B, S_q) + extra && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
       uint8_t* w = static_cast<uint8_t*>(workspace) + delta_bytes(B, S_q);
-      p.ld_ds = round_up(S_kv, 4);
-      p.ld_p = round_up(S_q, 64);
+      p.ld_k = round_up(S_kv, 4);
       p.ws_ds = reinterpret_cast<float*>(w);
-      p.ws_p = reinterpret_cast<float*>(w + round_up(B * S_q * p.ld_ds * 4, 256));
+      p.ws_p = reinterpret_cast<float*>(w + round_up(B * S_q * p.ld_k * 4, 256));
     }
     return launch_bwd_tf32(p, st, &t_launches);
   }

@@ -43,10 +43,10 @@ struct Params {
   uint64_t timeout_ns;
   uint32_t one;         // 1: an opaque multiplier for lcg_hi_at
   // fp32 backward with materialised gradients (workspace beyond delta, else
-  // null): dS [B, S_q, ld_ds] and P~^T = (dropout-scaled P)^T [B, S_kv, ld_p]
+  // null): dS and P~ = dropout-scaled P, both [B, S_q, ld_k]
   float* ws_ds;
   float* ws_p;
-  int64_t ld_ds, ld_p;
+  int64_t ld_k;
 };
 
 // CTA order of the tensor-core kernels over (batch row b, tile t): groups of

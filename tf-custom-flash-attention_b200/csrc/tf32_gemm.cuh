@@ -4,7 +4,7 @@
 //
 //   dQ[b] = scale * dS[b] K[b]        M = S_q rows,  K-dim = S_kv
 //   dK[b] = scale * dS[b]^T Q[b]      M = S_kv rows, K-dim = S_q (dS read MN-major)
-//   dV[b] =         P~^T[b] dO[b]     M = S_kv rows, K-dim = S_q
+//   dV[b] =         P~[b]^T dO[b]     M = S_kv rows, K-dim = S_q (P~ read MN-major)
 //
 // with dS = P (kf dP - D) and P~ = kf P, exactly the matrices the reference's
 // dQ and dK/dV kernels form element by element (sdpa/sdpa_bwd.cu.cc:125-170).
@@ -14,11 +14,13 @@
 // only fit N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
 //
 // One CTA = 128 rows of the result, all N columns.  Streams K-dim tiles of 32:
-// the A tile (128 x 32, K-major, 128-byte swizzle) and the B tile (32 x N,
-// MN-major, 32-byte swizzle atoms), both split in place into tf32 hi / lo by
-// four converter warps; one thread issues 4 x 3 SS MMAs per tile into one of
-// two TMEM accumulators, which 8 epilogue warps fold into an fp32 running
-// total every tile (the tensor cores' accumulation is not round-to-nearest).
+// the A tile (128 x 32) and the B tile (32 x N, MN-major, 32-byte swizzle
+// atoms) by TMA.  Four converter warps split A row by row into tf32 hi / lo
+// in TMEM and B in place in shared memory; one thread issues 4 x 3 TS MMAs
+// per tile (A from TMEM: only B is read from shared memory, whose bandwidth
+// bounded the all-shared-memory form) into one of two TMEM accumulators,
+// which 8 epilogue warps fold into an fp32 running total every tile (the
+// tensor cores' accumulation is not round-to-nearest).
 // Causal ranges: dQ row tile m0 needs keys < m0 + 128, dK / dV row tile m0
 // queries >= m0; every entry inside those ranges was written (masked ones as
 // zero).
@@ -59,18 +61,20 @@ struct GemmCfg {
   static constexpr int kK = 32;                          // K-dim per tile (one 128-byte row)
   static constexpr uint32_t kABytes = 128 * kK * 4;      // 16 KB
   static constexpr uint32_t kBBytes = kK * N * 4;        // N / 32 boxes of 32 x 32
-  static constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr uint32_t kStageBytes = kABytes + 2 * kBBytes;  // raw A, B hi, B lo
   static constexpr int kStages = 4 * kStageBytes <= 200 * 1024 ? 4 : 3;
   static constexpr uint32_t kBarOff = kStages * kStageBytes;
   static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
-  static constexpr uint32_t kTmemCols = 2 * N < 32 ? 32 : 2 * N;  // two accumulators
+  // TMEM: two accumulators (N columns each), then per stage A hi, A lo (32 each)
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kAslot0 = 2 * N;
+  static_assert(kAslot0 + kStages * 64 <= kTmemCols, "TMEM budget");
   static constexpr int kHC = N / 2;                      // columns per epilogue thread
   static_assert(N == 32 || N == 64 || N == 128, "N");
   static_assert(kSmemBytes <= 232448, "shared memory");
-  static __device__ __forceinline__ uint32_t a_hi(int s) { return s * kStageBytes; }
-  static __device__ __forceinline__ uint32_t a_lo(int s) { return s * kStageBytes + kABytes; }
-  static __device__ __forceinline__ uint32_t b_hi(int s) { return s * kStageBytes + 2 * kABytes; }
-  static __device__ __forceinline__ uint32_t b_lo(int s) { return s * kStageBytes + 2 * kABytes + kBBytes; }
+  static __device__ __forceinline__ uint32_t a_raw(int s) { return s * kStageBytes; }
+  static __device__ __forceinline__ uint32_t b_hi(int s) { return s * kStageBytes + kABytes; }
+  static __device__ __forceinline__ uint32_t b_lo(int s) { return s * kStageBytes + kABytes + kBBytes; }
 };
 
 struct GemmBarriers {
@@ -93,7 +97,7 @@ __device__ __forceinline__ void gemm_tmem_ld(uint32_t taddr, uint32_t* r) {
 // tm_a: 3-D map of the materialised matrix: K-major (A_MN false: K-dim
 // innermost, box 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN true: the
 // stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
-// atoms; dK reads dS this way).  tm_b: MN-major map of K, Q or dO, box 32
+// atoms; dK and dV read dS and P~ this way).  tm_b: MN-major map of K, Q or dO, box 32
 // columns x 32 K-dim.
 template <int N, bool HEADS, bool A_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -159,10 +163,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (A_MN) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            tma_load_3d(smem + Cfg::a_hi(s) + c * kK * 128, &tm_a, static_cast<int>(m0) + c * 32, k0,
+            tma_load_3d(smem + Cfg::a_raw(s) + c * kK * 128, &tm_a, static_cast<int>(m0) + c * 32, k0,
                         static_cast<int>(b), &bars->st_full[s]);
         } else {
-          tma_load_3d(smem + Cfg::a_hi(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
+          tma_load_3d(smem + Cfg::a_raw(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
         }
 #pragma unroll
         for (int c = 0; c < N / 32; ++c)
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------- MMA issuer
     if (lane == 0 && n > 0) {
       const uint32_t sb = smem_u32(smem);
-      constexpr uint32_t idesc = make_idesc(128, N, A_MN, true, true);
+      constexpr uint32_t idesc = make_idesc(128, N, false, true, true);  // A from TMEM
       for (int t = 0; t < n; ++t) {
         const int s = t % kStages, ab = t & 1;
         // accumulator ab was folded by the epilogue (its use t - 2)
@@ -195,17 +199,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         GEMM_PROBE_T0(w2);
         tc_fence_after();
         const uint32_t acc = tmem + ab * N;
+        const uint32_t ah = tmem + Cfg::kAslot0 + s * 64, al = ah + 32;
 #pragma unroll
         for (int kk = 0; kk < kK / 8; ++kk) {
-          const uint64_t ah = A_MN ? make_sw128_32b_desc(sb + Cfg::a_hi(s) + kk * 1024, kK * 128, 512)
-                                   : make_sw128_desc(sb + Cfg::a_hi(s) + kk * 32, 16, 1024);
-          const uint64_t al = A_MN ? make_sw128_32b_desc(sb + Cfg::a_lo(s) + kk * 1024, kK * 128, 512)
-                                   : make_sw128_desc(sb + Cfg::a_lo(s) + kk * 32, 16, 1024);
           const uint64_t bh = make_sw128_32b_desc(sb + Cfg::b_hi(s) + kk * 1024, kK * 128, 512);
           const uint64_t bl = make_sw128_32b_desc(sb + Cfg::b_lo(s) + kk * 1024, kK * 128, 512);
-          mma_tf32_ss(acc, ah, bh, idesc, kk > 0 ? 1u : 0u);  // a fresh accumulator every tile
-          mma_tf32_ss(acc, ah, bl, idesc, 1u);
-          mma_tf32_ss(acc, al, bh, idesc, 1u);
+          mma_tf32_ts(acc, ah + kk * 8, bh, idesc, kk > 0 ? 1u : 0u);  // a fresh accumulator every tile
+          mma_tf32_ts(acc, ah + kk * 8, bl, idesc, 1u);
+          mma_tf32_ts(acc, al + kk * 8, bh, idesc, 1u);
         }
         mma_commit(&bars->st_empty[s]);
         mma_commit(&bars->acc_full[ab]);
@@ -220,16 +221,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------- converters
+    // Thread tid owns A row tid (= its warp's TMEM lane quarter): it splits the
+    // row's 32 K-dim values into TMEM (the MMAs read A from there, sparing
+    // shared-memory bandwidth); all 128 split the B tile in place.
     const int tid = threadIdx.x - 256;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     for (int t = 0; t < n; ++t) {
       const int s = t % kStages;
       GEMM_PROBE_T0(c0);
       if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
       if (tid == 0) GEMM_PROBE_ADD(6, c0);
       GEMM_PROBE_T0(c1);
-      split_tile(smem + Cfg::a_hi(s), smem + Cfg::a_lo(s), Cfg::kABytes, tid, 128);
+      {
+        uint32_t h[32], l[32];
+        const uint8_t* a = smem + Cfg::a_raw(s);
+        if (A_MN) {  // box tid / 32, element tid % 32 of each 128-byte K row (32-byte atoms, XOR row & 3)
+          const uint8_t* box = a + (tid >> 5) * (kK * 128) + ((lane & 7) << 2);
+#pragma unroll
+          for (int k = 0; k < kK; ++k) {
+            float hi, lo;
+            split_tf32(*reinterpret_cast<const float*>(box + k * 128 + ((((lane >> 3) ^ (k & 3))) << 5)), hi, lo);
+            h[k] = __float_as_uint(hi);
+            l[k] = __float_as_uint(lo);
+          }
+        } else {  // row tid: 16-byte chunk j at chunk j ^ (row & 7) (128-byte swizzle)
+          const uint8_t* row = a + tid * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (tid & 7)) << 4));
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float hi, lo;
+              split_tf32(xv[e], hi, lo);
+              h[4 * j + e] = __float_as_uint(hi);
+              l[4 * j + e] = __float_as_uint(lo);
+            }
+          }
+        }
+        const uint32_t ta = tmem + lane_base + Cfg::kAslot0 + s * 64;
+        SDPA_TMEM_ST32(ta, h);
+        SDPA_TMEM_ST32(ta + 32, l);
+      }
       split_tile(smem + Cfg::b_hi(s), smem + Cfg::b_lo(s), Cfg::kBBytes, tid, 128);
+      tmem_wait_st();
       fence_proxy_async_smem();
+      tc_fence_before();
       if (tid == 0) GEMM_PROBE_ADD(7, c1);
       mbar_arrive(&bars->st_ready[s]);
     }

@@ -5,7 +5,7 @@
 //   S^T = K Q^T, dP^T = V dO^T          (TS MMAs, 3xTF32, into one TMEM buffer)
 //   P~ = kf p, dS = p (kf dP - D)       (8 elementwise warps; p = exp(S - lse))
 //
-// and writes dS [B, S_q, ld_ds] and P~^T [B, S_kv, ld_p] to the workspace,
+// and writes dS and P~, both [B, S_q, ld_k], to the workspace,
 // where the three GEMMs of tf32_gemm.cuh turn them into dQ, dK and dV.  The
 // elementwise formulas, skip rule (p <= 1e-6) and dropout counters are the
 // reference's dK/dV kernel's (sdpa/sdpa_bwd.cu.cc:125-170), as in the passes
@@ -30,6 +30,17 @@ namespace tf32 {
 
 constexpr int kScoreThreads = 448;
 
+// Timing probe for tuning builds (-DSDPA_B200_TF32_PROBE=4): SM cycles of
+// CTA 0's roles, as in the passes.
+#if defined(SDPA_B200_TF32_PROBE) && SDPA_B200_TF32_PROBE == 4
+#define SCORE_PROBE_T0(v) const long long v = clock64()
+#define SCORE_PROBE_ADD(slot, t0) \
+  if (blockIdx.x == 0) atomicAdd(&g_tf32_probe[slot], static_cast<unsigned long long>(clock64() - (t0)))
+#else
+#define SCORE_PROBE_T0(v)
+#define SCORE_PROBE_ADD(slot, t0)
+#endif
+
 template <int DQK, int DV>
 struct ScoreCfg {
   // TMEM columns: K hi / lo, V hi / lo, then S^T (kN) and dP^T (kN)
@@ -39,24 +50,30 @@ struct ScoreCfg {
   static constexpr int kHalf = kN / 2;
   static_assert(kT + 2 * kN <= 512, "TMEM budget");
   // shared memory per stage: Q hi, Q lo (kN x DQK), dO hi, dO lo (kN x DV),
-  // K-major with 128-byte swizzle, then lse (log2 units) and D of the kN rows
+  // K-major with 128-byte swizzle.  lse (log2 units) and D of a tile's kN
+  // rows sit in a separate ring of kVecSlots, so that a stage is free for the
+  // next load as soon as its MMAs complete, while the elementwise warps still
+  // read the tile's lse / D.
   static constexpr uint32_t kQBytes = kN * DQK * 4, kOBytes = kN * DV * 4;
-  static constexpr uint32_t kStageBytes = 2 * kQBytes + 2 * kOBytes + 2 * kN * 4;
+  static constexpr uint32_t kStageBytes = 2 * kQBytes + 2 * kOBytes;
   static constexpr uint32_t kStageAligned = (kStageBytes + 1023) / 1024 * 1024;
   static constexpr int kStages = 3 * kStageAligned <= 200 * 1024 ? 3 : 2;
-  static constexpr uint32_t kBarOff = kStages * kStageAligned;
+  static constexpr int kVecSlots = 4;
+  static constexpr uint32_t kVecOff = kStages * kStageAligned;
+  static constexpr uint32_t kBarOff = kVecOff + kVecSlots * 2 * kN * 4;
   static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory");
   static __device__ __forceinline__ uint32_t q_hi(int s) { return s * kStageAligned; }
   static __device__ __forceinline__ uint32_t q_lo(int s) { return s * kStageAligned + kQBytes; }
   static __device__ __forceinline__ uint32_t o_hi(int s) { return s * kStageAligned + 2 * kQBytes; }
   static __device__ __forceinline__ uint32_t o_lo(int s) { return s * kStageAligned + 2 * kQBytes + kOBytes; }
-  static __device__ __forceinline__ uint32_t vec(int s) { return s * kStageAligned + 2 * kQBytes + 2 * kOBytes; }
+  static __device__ __forceinline__ uint32_t vec(int v) { return kVecOff + v * 2 * kN * 4; }
 };
 
 struct ScoreBarriers {
   uint64_t res_ready;
   uint64_t st_full[3], st_ready[3], st_empty[3];
+  uint64_t vec_full[4], vec_empty[4];
   uint64_t s_full, t_free;
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -90,7 +107,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->st_full[s], 1);
       mbar_init(&bars->st_ready[s], 128);
-      mbar_init(&bars->st_empty[s], 1 + 256);  // the tile's MMAs, and every elementwise thread done with lse / D
+      mbar_init(&bars->st_empty[s], 1);
+    }
+    for (int v = 0; v < Cfg::kVecSlots; ++v) {
+      mbar_init(&bars->vec_full[v], 128);
+      mbar_init(&bars->vec_empty[v], 256);
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->t_free, 256);
@@ -115,7 +136,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       int issued = 0;
       for (int t = 0; t < n; ++t) {
         const int s = t % kStages;
+        SCORE_PROBE_T0(p0);
         if (!mbar_wait(&bars->st_empty[s], ((t / kStages) & 1) ^ 1, ctl)) break;
+        SCORE_PROBE_ADD(8, p0);
         const int row0 = (tile0 + t) * kN;
         mbar_expect_tx(&bars->st_full[s], Cfg::kQBytes + Cfg::kOBytes);
 #pragma unroll
@@ -144,13 +167,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       for (int t = 0; ok && t < n; ++t) {
         const int s = t % kStages;
         // the buffer is free once every elementwise thread loaded tile t - 1
+        SCORE_PROBE_T0(w0);
         if (t > 0 && !mbar_wait(&bars->t_free, (t - 1) & 1, ctl)) break;
+        SCORE_PROBE_ADD(0, w0);
+        SCORE_PROBE_T0(w1);
         if (!mbar_wait(&bars->st_ready[s], (t / kStages) & 1, ctl)) break;
+        SCORE_PROBE_ADD(1, w1);
+        SCORE_PROBE_T0(w2);
         tc_fence_after();
         issue_scores<DQK, kN>(tT, tmem + Cfg::kKh, tmem + Cfg::kKl, sb + Cfg::q_hi(s), sb + Cfg::q_lo(s));
         issue_scores<DV, kN>(tT + kN, tmem + Cfg::kVh, tmem + Cfg::kVl, sb + Cfg::o_hi(s), sb + Cfg::o_lo(s));
         mma_commit(&bars->s_full);
         mma_commit(&bars->st_empty[s]);
+        SCORE_PROBE_ADD(2, w2);
       }
       mma_commit(&bars->mma_done);
       WaitCtl drain = ctl;
@@ -164,15 +193,22 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int tid = threadIdx.x - 256;
     for (int t = 0; t < n; ++t) {
       const int s = t % kStages;
+      SCORE_PROBE_T0(c0);
       if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
-      float* vec = reinterpret_cast<float*>(smem + Cfg::vec(s));
+      if (tid == 0) SCORE_PROBE_ADD(6, c0);
+      SCORE_PROBE_T0(c1);
+      const int vs = t % Cfg::kVecSlots;
+      if (!tc::warp_wait(&bars->vec_empty[vs], ((t / Cfg::kVecSlots) & 1) ^ 1, ctl)) break;
+      float* vec = reinterpret_cast<float*>(smem + Cfg::vec(vs));
       const int64_t i = static_cast<int64_t>(tile0 + t) * kN + (tid % kN);
       const bool in = i < p.S_q;
       if (tid < kN) vec[tid] = in ? p.lse[b * p.S_q + i] * kLog2e : INFINITY;  // p = 0 beyond S_q
       else if (tid < 2 * kN) vec[tid] = in ? p.delta[b * p.S_q + i] : 0.0f;
+      mbar_arrive(&bars->vec_full[vs]);
       split_tile(smem + Cfg::q_hi(s), smem + Cfg::q_lo(s), Cfg::kQBytes, tid, 128);
       split_tile(smem + Cfg::o_hi(s), smem + Cfg::o_lo(s), Cfg::kOBytes, tid, 128);
       fence_proxy_async_smem();
+      if (tid == 0) SCORE_PROBE_ADD(7, c1);
       mbar_arrive(&bars->st_ready[s]);
     }
   } else {
@@ -185,6 +221,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const bool row_ok = rr < p.S_kv;
     const float sl2 = p.scale_log2, dp_inv = p.dp_inv;
     const uint32_t thr_m1 = drop_thr_m1(p.drop_thr);
+    SCORE_PROBE_T0(e9);
     {  // K and V rows to TMEM (hi / lo): this thread's half of the columns
       const float* krow = static_cast<const float*>(p.k) + (row_ok ? row_offset_t<HEADS>(p.H, b, rr, p.S_kv, p.D_qk) : 0);
 #pragma unroll
@@ -205,12 +242,17 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       tc_fence_before();
       mbar_arrive(&bars->res_ready);
     }
+    if (threadIdx.x == 0) SCORE_PROBE_ADD(9, e9);
     const uint64_t step_i = static_cast<uint64_t>(p.S_kv) * kLcgA;  // counter step between query rows
     const uint32_t step_lo = static_cast<uint32_t>(step_i), step_hi = static_cast<uint32_t>(step_i >> 32);
     for (int t = 0; t < n; ++t) {
-      const int s = t % kStages;
-      if (!tc::warp_wait(&bars->s_full, t & 1, ctl) || !tc::warp_wait(&bars->st_ready[s], (t / kStages) & 1, ctl))
+      SCORE_PROBE_T0(e0);
+      const int vs = t % Cfg::kVecSlots;
+      if (!tc::warp_wait(&bars->s_full, t & 1, ctl) ||
+          !tc::warp_wait(&bars->vec_full[vs], (t / Cfg::kVecSlots) & 1, ctl))
         break;
+      if (threadIdx.x == 0) SCORE_PROBE_ADD(4, e0);
+      SCORE_PROBE_T0(e1);
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + Cfg::kT + col0;
       uint32_t sv[kHalf], dpv[kHalf];
@@ -221,7 +263,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       mbar_arrive(&bars->t_free);
       // columns are query rows i = c0g + c of key row j = rr
       const int64_t c0g = static_cast<int64_t>(tile0 + t) * kN + col0;
-      const float* vec = reinterpret_cast<const float*>(smem + Cfg::vec(s)) + col0;
+      const float* vec = reinterpret_cast<const float*>(smem + Cfg::vec(vs)) + col0;
       int lo = -1;  // causal: column c valid iff c0g + c >= j
       if (p.causal) {
         const int64_t d = rr - c0g;
@@ -230,12 +272,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       LcgWalk st(DROP ? lcg_state(p.rng_base + static_cast<uint64_t>(b * p.S_q + c0g) * static_cast<uint64_t>(p.S_kv),
                                   static_cast<uint64_t>(rr))
                       : 0);
-      // P~^T row j, columns c0g.. (ld_p covers every streamed column); dS column
-      // j of query rows c0g.. (consecutive lanes write consecutive keys)
-      float* const p_row = p.ws_p + (b * p.S_kv + rr) * p.ld_p + c0g;
-      float* const ds_col = p.ws_ds + (b * p.S_q + c0g) * p.ld_ds + rr;
+      // column j of dS and P~, query rows c0g.. < S_q: consecutive lanes write
+      // consecutive keys, so each store of a warp fills one 128-byte line
+      // (rows of a thread's own, written with vector stores, would touch 32
+      // lines per store and measured 1.5x slower)
+      const int64_t col_off = (b * p.S_q + c0g) * p.ld_k + rr;
+      float* const ds_col = p.ws_ds + col_off;
+      float* const p_col = p.ws_p + col_off;
       const int lim = static_cast<int>(p.S_q - c0g < kHalf ? p.S_q - c0g : kHalf);
-      float pk4[4];
 #pragma unroll
       for (int c = 0; c < kHalf; ++c) {
         float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -vec[c]));
@@ -245,13 +289,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           kf = st.dropped(thr_m1) ? 0.0f : dp_inv;
           st.step(step_lo, step_hi);
         }
-        pk4[c & 3] = pr * kf;
-        if (row_ok) {
-          if ((c & 3) == 3) *reinterpret_cast<float4*>(p_row + c - 3) = make_float4(pk4[0], pk4[1], pk4[2], pk4[3]);
-          if (c < lim) ds_col[static_cast<int64_t>(c) * p.ld_ds] = pr * fmaf(kf, __uint_as_float(dpv[c]), -vec[kN + c]);
+        if (row_ok && c < lim) {
+          p_col[static_cast<int64_t>(c) * p.ld_k] = pr * kf;
+          ds_col[static_cast<int64_t>(c) * p.ld_k] = pr * fmaf(kf, __uint_as_float(dpv[c]), -vec[kN + c]);
         }
       }
-      mbar_arrive(&bars->st_empty[s]);
+      if (threadIdx.x == 0) SCORE_PROBE_ADD(5, e1);
+      mbar_arrive(&bars->vec_empty[vs]);
     }
   }
   tc_fence_before();

@@ -120,7 +120,8 @@ int launch_scores(const Params& p, cudaStream_t st, int* launches) {
 }
 
 // The GEMM route (p.ws_ds / p.ws_p set): D, the score pass writing dS and
-// P~^T, then dQ = scale dS K, dK = scale dS^T Q and dV = P~^T dO as GEMMs.
+// P~, then dQ = scale dS K, dK = scale dS^T Q and dV = P~^T dO as GEMMs (the
+// last two read their A operand MN-major).
 template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
   sdpa_b200::record_bwd_event(0, st);
@@ -131,15 +132,15 @@ int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
   if (int r = launch_scores<DQK, DV, DROP, HEADS>(p, st, launches)) return r;
   sdpa_b200::record_bwd_event(1, st);
   const int range_q = p.causal ? 1 : 0, range_kv = p.causal ? 2 : 0;
-  if (int r = launch_gemm<DQK, HEADS, false>(p.ws_ds, p.ld_ds, p.k, p.D_qk, static_cast<float*>(p.dq), p, p.S_q,
+  if (int r = launch_gemm<DQK, HEADS, false>(p.ws_ds, p.ld_k, p.k, p.D_qk, static_cast<float*>(p.dq), p, p.S_q,
                                              p.S_kv, p.scale, range_q, st, launches))
     return r;
   sdpa_b200::record_bwd_event(2, st);
-  if (int r = launch_gemm<DQK, HEADS, true>(p.ws_ds, p.ld_ds, p.q, p.D_qk, static_cast<float*>(p.dk), p, p.S_kv,
+  if (int r = launch_gemm<DQK, HEADS, true>(p.ws_ds, p.ld_k, p.q, p.D_qk, static_cast<float*>(p.dk), p, p.S_kv,
                                             p.S_q, p.scale, range_kv, st, launches))
     return r;
   sdpa_b200::record_bwd_event(3, st);
-  if (int r = launch_gemm<DV, HEADS, false>(p.ws_p, p.ld_p, p.d_o, p.D_v, static_cast<float*>(p.dv), p, p.S_kv,
+  if (int r = launch_gemm<DV, HEADS, true>(p.ws_p, p.ld_k, p.d_o, p.D_v, static_cast<float*>(p.dv), p, p.S_kv,
                                             p.S_q, 1.0f, range_kv, st, launches))
     return r;
   sdpa_b200::record_bwd_event(4, st);
