@@ -129,6 +129,19 @@ inline cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& do
   return e;
 }
 
+// SM count of the current device (cached per device ordinal), for persistent grids.
+inline int num_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int v = cache[dev & 63].load();
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev & 63].store(v);
+  }
+  return v;
+}
+
 inline int launch_result() {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SDPA_B200_OK : cuda_failure("kernel launch", e);

@@ -13,7 +13,8 @@
 // three tf32 MMAs, and with hi / lo operands resident the recomputing passes
 // only fit N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
 //
-// One CTA = 128 rows of the result, all N columns.  Streams K-dim tiles of 32:
+// A work item = 128 rows of the result, all N columns; persistent CTAs take
+// items in turn (below).  Streams K-dim tiles of 32:
 // the A tile (128 x 32) and the B tile (32 x N, MN-major, 32-byte swizzle
 // atoms) by TMA.  Four converter warps split A row by row into tf32 hi / lo
 // in TMEM and B in place in shared memory; one thread issues 4 x 3 TS MMAs
@@ -99,6 +100,44 @@ __device__ __forceinline__ void gemm_tmem_ld(uint32_t taddr, uint32_t* r) {
 // stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
 // atoms; dK and dV read dS and P~ this way).  tm_b: MN-major map of K, Q or dO, box 32
 // columns x 32 K-dim.
+// One work item = 128 result rows of one batch row: its K-dim tiles [tile0,
+// tile0 + n) (causal ranges) and its TMA coordinates.
+struct GemmItem {
+  int64_t b, m0;
+  int hb, ob, tile0, n;
+};
+template <bool HEADS>
+__device__ __forceinline__ GemmItem gemm_item(const GemmArgs& g, int64_t item, int kK) {
+  GemmItem it;
+  const int64_t n_mt = (g.M + 127) / 128;
+  int64_t tord;
+  raster(item, g.B, n_mt, it.b, tord);
+  it.hb = HEADS ? static_cast<int>(it.b % g.H) : 0;
+  it.ob = HEADS ? static_cast<int>(it.b / g.H) : static_cast<int>(it.b);
+  // heaviest causal row tiles first: high ones for dQ, low ones for dK / dV
+  it.m0 = (g.range == 1 ? n_mt - 1 - tord : tord) * 128;
+  const int64_t n_all = (g.K + kK - 1) / kK;
+  it.tile0 = 0;
+  it.n = static_cast<int>(n_all);
+  if (g.range == 1) {
+    it.n = static_cast<int>(min(n_all, (it.m0 + 127) / kK + 1));
+  } else if (g.range == 2) {
+    it.tile0 = static_cast<int>(it.m0 / kK);
+    it.n = static_cast<int>(n_all - it.tile0 > 0 ? n_all - it.tile0 : 0);
+  }
+  return it;
+}
+
+// Persistent: CTA c takes work items c, c + gridDim.x, ... (heaviest first),
+// and every role runs one continuous pipeline over the concatenated K-dim
+// tiles of its items (index q), so a short item (dK / dV: 16 tiles at cfg5)
+// does not pay the pipeline's fill and drain, and the epilogue of one item
+// overlaps the next item's loads and MMAs.
+// tm_a: 3-D map of the materialised matrix: K-major (A_MN false: K-dim
+// innermost, box 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN true: the
+// stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
+// atoms; dK and dV read dS and P~ this way).  tm_b: MN-major map of K, Q or
+// dO, box 32 columns x 32 K-dim.
 template <int N, bool HEADS, bool A_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
@@ -108,21 +147,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = tc::align1024(smem_raw);
   GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-
-  const int64_t n_mt = (g.M + 127) / 128;
-  int64_t b, tord;
-  raster(blockIdx.x, g.B, n_mt, b, tord);
-  const int hb = HEADS ? static_cast<int>(b % g.H) : 0, ob = HEADS ? static_cast<int>(b / g.H) : static_cast<int>(b);
-  // heaviest causal row tiles first: high ones for dQ, low ones for dK / dV
-  const int64_t m0 = (g.range == 1 ? n_mt - 1 - tord : tord) * 128;
-  const int64_t n_all = (g.K + kK - 1) / kK;
-  int tile0 = 0, n = static_cast<int>(n_all);
-  if (g.range == 1) {
-    n = static_cast<int>(min(n_all, (m0 + 127) / kK + 1));
-  } else if (g.range == 2) {
-    tile0 = static_cast<int>(m0 / kK);
-    n = static_cast<int>(n_all - tile0 > 0 ? n_all - tile0 : 0);
-  }
+  const int64_t n_items = ((g.M + 127) / 128) * g.B;
+  int n_tiles = 0;  // K-dim tiles of all this CTA's items
+  for (int64_t item = blockIdx.x; item < n_items; item += gridDim.x) n_tiles += gemm_item<HEADS>(g, item, kK).n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -149,52 +176,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 12) {
     // ------------------------------------------------------ TMA producer
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
-      int issued = 0;
-      for (int t = 0; t < n; ++t) {
-        const int s = t % kStages;
-        GEMM_PROBE_T0(p0);
-        if (!mbar_wait(&bars->st_empty[s], ((t / kStages) & 1) ^ 1, ctl)) break;
-        GEMM_PROBE_ADD(8, p0);
-        const int k0 = (tile0 + t) * kK;
-        mbar_expect_tx(&bars->st_full[s], Cfg::kABytes + Cfg::kBBytes);
-        if (A_MN) {
+      int q = 0;  // tiles issued
+      bool ok = true;
+      for (int64_t item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const GemmItem it = gemm_item<HEADS>(g, item, kK);
+        for (int t = 0; t < it.n; ++t, ++q) {
+          const int s = q % kStages;
+          GEMM_PROBE_T0(p0);
+          if (!mbar_wait(&bars->st_empty[s], ((q / kStages) & 1) ^ 1, ctl)) {
+            ok = false;
+            break;
+          }
+          GEMM_PROBE_ADD(8, p0);
+          const int k0 = (it.tile0 + t) * kK;
+          mbar_expect_tx(&bars->st_full[s], Cfg::kABytes + Cfg::kBBytes);
+          if (A_MN) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tma_load_3d(smem + Cfg::a_raw(s) + c * kK * 128, &tm_a, static_cast<int>(m0) + c * 32, k0,
-                        static_cast<int>(b), &bars->st_full[s]);
-        } else {
-          tma_load_3d(smem + Cfg::a_raw(s), &tm_a, k0, static_cast<int>(m0), static_cast<int>(b), &bars->st_full[s]);
+            for (int c = 0; c < 4; ++c)
+              tma_load_3d(smem + Cfg::a_raw(s) + c * kK * 128, &tm_a, static_cast<int>(it.m0) + c * 32, k0,
+                          static_cast<int>(it.b), &bars->st_full[s]);
+          } else {
+            tma_load_3d(smem + Cfg::a_raw(s), &tm_a, k0, static_cast<int>(it.m0), static_cast<int>(it.b),
+                        &bars->st_full[s]);
+          }
+#pragma unroll
+          for (int c = 0; c < N / 32; ++c)
+            tma_load_rows(smem + Cfg::b_hi(s) + c * kK * 128, &tm_b, c * 32, k0, it.hb, it.ob, &bars->st_full[s],
+                          HEADS);
         }
-#pragma unroll
-        for (int c = 0; c < N / 32; ++c)
-          tma_load_rows(smem + Cfg::b_hi(s) + c * kK * 128, &tm_b, c * 32, k0, hb, ob, &bars->st_full[s], HEADS);
-        issued = t + 1;
       }
       if (*ctl.abort_flag) {  // let the copies in flight land before the CTA exits
         WaitCtl drain = ctl;
         drain.deadline_ns = globaltimer_ns() + g.timeout_ns;
         int dummy = 0;
         drain.abort_flag = &dummy;
-        for (int t = (issued > kStages ? issued - kStages : 0); t < issued; ++t)
+        for (int t = (q > kStages ? q - kStages : 0); t < q; ++t)
           mbar_wait(&bars->st_full[t % kStages], (t / kStages) & 1, drain);
       }
     }
   } else if (warp == 13) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       const uint32_t sb = smem_u32(smem);
       constexpr uint32_t idesc = make_idesc(128, N, false, true, true);  // A from TMEM
-      for (int t = 0; t < n; ++t) {
-        const int s = t % kStages, ab = t & 1;
-        // accumulator ab was folded by the epilogue (its use t - 2)
+      for (int q = 0; q < n_tiles; ++q) {
+        const int s = q % kStages, ab = q & 1;
+        // accumulator ab was folded by the epilogue (its use q - 2)
         GEMM_PROBE_T0(w0);
-        if (t >= 2 && !mbar_wait(&bars->acc_empty[ab], ((t >> 1) - 1) & 1, ctl)) break;
+        if (q >= 2 && !mbar_wait(&bars->acc_empty[ab], ((q >> 1) - 1) & 1, ctl)) break;
         GEMM_PROBE_ADD(0, w0);
         GEMM_PROBE_T0(w1);
-        if (!mbar_wait(&bars->st_ready[s], (t / kStages) & 1, ctl)) break;
+        if (!mbar_wait(&bars->st_ready[s], (q / kStages) & 1, ctl)) break;
         GEMM_PROBE_ADD(1, w1);
         GEMM_PROBE_T0(w2);
         tc_fence_after();
@@ -222,47 +257,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp >= 8) {
     // ------------------------------------------------------- converters
     // Thread tid owns A row tid (= its warp's TMEM lane quarter): it splits the
-    // row's 32 K-dim values into TMEM (the MMAs read A from there, sparing
-    // shared-memory bandwidth); all 128 split the B tile in place.
+    // row's 32 K-dim values into TMEM, where the MMAs read A (sparing shared-
+    // memory bandwidth); all 128 split the B tile in place.  (Splitting B in
+    // the epilogue warps instead measured no faster.)
     const int tid = threadIdx.x - 256;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    for (int t = 0; t < n; ++t) {
-      const int s = t % kStages;
+    for (int q = 0; q < n_tiles; ++q) {
+      const int s = q % kStages;
       GEMM_PROBE_T0(c0);
-      if (!tc::warp_wait(&bars->st_full[s], (t / kStages) & 1, ctl)) break;
+      if (!tc::warp_wait(&bars->st_full[s], (q / kStages) & 1, ctl)) break;
       if (tid == 0) GEMM_PROBE_ADD(6, c0);
       GEMM_PROBE_T0(c1);
-      {
-        uint32_t h[32], l[32];
-        const uint8_t* a = smem + Cfg::a_raw(s);
-        if (A_MN) {  // box tid / 32, element tid % 32 of each 128-byte K row (32-byte atoms, XOR row & 3)
-          const uint8_t* box = a + (tid >> 5) * (kK * 128) + ((lane & 7) << 2);
+      uint32_t h[32], l[32];
+      const uint8_t* a = smem + Cfg::a_raw(s);
+      if (A_MN) {  // box tid / 32, element tid % 32 of each 128-byte K row (32-byte atoms, XOR row & 3)
+        const uint8_t* box = a + (tid >> 5) * (kK * 128) + ((lane & 7) << 2);
 #pragma unroll
-          for (int k = 0; k < kK; ++k) {
+        for (int k = 0; k < kK; ++k) {
+          float hi, lo;
+          split_tf32(*reinterpret_cast<const float*>(box + k * 128 + (((lane >> 3) ^ (k & 3)) << 5)), hi, lo);
+          h[k] = __float_as_uint(hi);
+          l[k] = __float_as_uint(lo);
+        }
+      } else {  // row tid: 16-byte chunk j at chunk j ^ (row & 7) (128-byte swizzle)
+        const uint8_t* row = a + tid * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (tid & 7)) << 4));
+          const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
             float hi, lo;
-            split_tf32(*reinterpret_cast<const float*>(box + k * 128 + ((((lane >> 3) ^ (k & 3))) << 5)), hi, lo);
-            h[k] = __float_as_uint(hi);
-            l[k] = __float_as_uint(lo);
-          }
-        } else {  // row tid: 16-byte chunk j at chunk j ^ (row & 7) (128-byte swizzle)
-          const uint8_t* row = a + tid * 128;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (tid & 7)) << 4));
-            const float xv[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float hi, lo;
-              split_tf32(xv[e], hi, lo);
-              h[4 * j + e] = __float_as_uint(hi);
-              l[4 * j + e] = __float_as_uint(lo);
-            }
+            split_tf32(xv[e], hi, lo);
+            h[4 * j + e] = __float_as_uint(hi);
+            l[4 * j + e] = __float_as_uint(lo);
           }
         }
-        const uint32_t ta = tmem + lane_base + Cfg::kAslot0 + s * 64;
-        SDPA_TMEM_ST32(ta, h);
-        SDPA_TMEM_ST32(ta + 32, l);
       }
+      const uint32_t ta = tmem + lane_base + Cfg::kAslot0 + s * 64;
+      SDPA_TMEM_ST32(ta, h);
+      SDPA_TMEM_ST32(ta + 32, l);
       split_tile(smem + Cfg::b_hi(s), smem + Cfg::b_lo(s), Cfg::kBBytes, tid, 128);
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -272,20 +306,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ---------------------------------------------------- epilogue warps
+    // Tile q's accumulator is folded into the running total of its item; the
+    // item's rows are written after its last tile.
     const int half = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int64_t f_item = blockIdx.x;  // the item being folded, and its next tile
+    GemmItem f_it = gemm_item<HEADS>(g, f_item < n_items ? f_item : 0, kK);
+    int f_t = 0;
     float tot[kHC];
 #pragma unroll
     for (int e = 0; e < kHC; ++e) tot[e] = 0.0f;
-    bool ok = true;
-    for (int t = 0; t < n; ++t) {
-      const int ab = t & 1;
+    for (int qf = 0; qf < n_tiles; ++qf) {
+      const int ab = qf & 1;
       GEMM_PROBE_T0(e0);
-      if (!tc::warp_wait(&bars->acc_full[ab], (t >> 1) & 1, ctl)) {
-        ok = false;
-        break;
-      }
+      if (!tc::warp_wait(&bars->acc_full[ab], (qf >> 1) & 1, ctl)) break;
       if (threadIdx.x == 0) GEMM_PROBE_ADD(4, e0);
       GEMM_PROBE_T0(e1);
       tc_fence_after();
@@ -301,17 +336,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       if (threadIdx.x == 0) GEMM_PROBE_ADD(5, e1);
       mbar_arrive(&bars->acc_empty[ab]);
-    }
-    const int64_t m = m0 + r;
-    if (ok && m < g.M) {
-      float* crow = g.c + row_offset_t<HEADS>(g.H, b, m, g.M, g.D);
+      if (++f_t < f_it.n) continue;
+      // last tile of the item: its rows (every item has n >= 1: K >= 1, and the
+      // causal ranges start at or before the row tile's diagonal)
+      const int64_t m = f_it.m0 + r;
+      if (m < g.M) {
+        float* crow = g.c + row_offset_t<HEADS>(g.H, f_it.b, m, g.M, g.D);
 #pragma unroll
-      for (int q = 0; q < kHC / 4; ++q) {
-        const int col = half * kHC + 4 * q;
-        if (col < g.D)
-          *reinterpret_cast<float4*>(crow + col) = make_float4(tot[4 * q] * g.alpha, tot[4 * q + 1] * g.alpha,
-                                                               tot[4 * q + 2] * g.alpha, tot[4 * q + 3] * g.alpha);
+        for (int c4 = 0; c4 < kHC / 4; ++c4) {
+          const int col = half * kHC + 4 * c4;
+          if (col < g.D)
+            *reinterpret_cast<float4*>(crow + col) =
+                make_float4(tot[4 * c4] * g.alpha, tot[4 * c4 + 1] * g.alpha, tot[4 * c4 + 2] * g.alpha,
+                            tot[4 * c4 + 3] * g.alpha);
+        }
       }
+#pragma unroll
+      for (int e = 0; e < kHC; ++e) tot[e] = 0.0f;
+      f_item += gridDim.x;
+      if (f_item < n_items) f_it = gemm_item<HEADS>(g, f_item, kK);
+      f_t = 0;
     }
   }
   tc_fence_before();

@@ -95,8 +95,12 @@ int launch_gemm(const float* a, int64_t ld, const void* b_src, int d_b, float* c
   g.alpha = alpha;
   g.range = range;
   g.timeout_ns = p.timeout_ns;
-  const int64_t grid = ((M + 127) / 128) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  // Persistent (one CTA per SM: the shared memory admits no second) for short
+  // items, whose pipeline fill and drain it hides; long items (dQ at cfg5: 128
+  // tiles) run one CTA each, which the hardware balances better than a
+  // static round-robin (measured).
+  const int64_t items = ((M + 127) / 128) * p.B;
+  const int64_t grid = (K + Cfg::kK - 1) / Cfg::kK >= 64 || items < num_sms() ? items : num_sms();
   kern<<<static_cast<unsigned>(grid), tf32::kGemmThreads, Cfg::kSmemBytes, st>>>(ma, mb, g);
   ++*launches;
   return launch_result();
