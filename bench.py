@@ -81,6 +81,25 @@ def peaks():
         return 1590.0, "fallback"
 
 
+def hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def min_bytes(w, B, S_q, S_kv, esize):
+    """Bytes one fwd + bwd step must move at least: the forward reads Q, K, V and
+    writes O and stats; the backward reads Q, K, V, O, dO and stats and writes
+    dQ, dK, dV (a small shape's step is bound by latency, not by these)."""
+    q, k, v, o = (B * S_q * w["D_qk"], B * S_kv * w["D_qk"], B * S_kv * w["D_v"], B * S_q * w["D_v"])
+    stats = B * S_q * 4
+    fwd = (q + k + v + o) * esize + stats
+    bwd = (q + k + v + 2 * o) * esize + stats + (q + k + v) * esize
+    return fwd + bwd
+
+
 class ClockSampler:
     """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
 
@@ -504,6 +523,8 @@ def run_ours(args, w):
             cpu = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample_txt}
         except Exception as e:  # the reference build is missing on this box
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    hbm = hbm_peak()
+    mb = min_bytes(w, B, S, S_kv, 2 if dt == torch.float16 else 4)  # this rank's share
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -520,6 +541,8 @@ def run_ours(args, w):
         "roofline": {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic, "ms_per_launch": kms,
                      "flops_per_launch": kfl, "kernel_ms": kernel_ms},
+        "memory": {"min_bytes_per_step": mb, "achieved_gbs": mb / (ms * 1e-3) / 1e9, "peak_gbs": hbm[0],
+                   "peak_kind": hbm[1], "frac": mb / (ms * 1e-3) / 1e9 / hbm[0]},
         "e2e": {"value": (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "bound": "pinned host<->device copies (see per_rank copy GB/s)"},

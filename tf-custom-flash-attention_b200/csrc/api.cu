@@ -216,7 +216,7 @@ static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int
   if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
   if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return 0;
   const size_t one = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
-  return 2 * one <= kGemmWorkspaceCap ? 2 * one : 0;
+  return 2 * one <= kGemmWorkspaceCap ? 2 * one + 256 : 0;  // + room to align the start to 256 bytes
 }
 
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
@@ -258,8 +258,9 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
   if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) {
     const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
-    if (extra && workspace_bytes >= delta_bytes(B, S_q) + extra && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
-      uint8_t* w = static_cast<uint8_t*>(workspace) + delta_bytes(B, S_q);
+    if (extra && workspace_bytes >= delta_bytes(B, S_q) + extra) {
+      const uintptr_t w0 = reinterpret_cast<uintptr_t>(workspace) + delta_bytes(B, S_q);
+      uint8_t* w = reinterpret_cast<uint8_t*>((w0 + 255u) & ~uintptr_t(255u));
       p.ld_k = round_up(S_kv, 4);
       p.ws_ds = reinterpret_cast<float*>(w);
       p.ws_p = reinterpret_cast<float*>(w + round_up(B * S_q * p.ld_k * 4, 256));
