@@ -29,18 +29,20 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
-def bwd(q, k, v, o, s, do, kw, minimal):
+def bwd(q, k, v, o, s, do, kw, minimal, ws_shift=0):
+    """ws_shift: bytes by which the workspace start is moved off torch's
+    256-byte alignment (TF's allocator guarantees only 64)."""
     L = fa._lib.lib()
     B, S_q, D_qk = q.shape
     S_kv, D_v = k.shape[1], v.shape[2]
     full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, D_qk, D_v)
     n = B * S_q * 4 if minimal else full
     assert minimal or full > B * S_q * 4  # the GEMM route applies to these shapes
-    ws = torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+    ws = torch.empty((n + ws_shift + 3) // 4, dtype=torch.float32, device="cuda")
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     rc = L.sdpa_b200_bwd(fa._lib.F32, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), s.data_ptr(),
                          do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
-                         kw["scale"], kw["dropout"], int(kw["causal_mask"]), 5, 9, ws.data_ptr(), n,
+                         kw["scale"], kw["dropout"], int(kw["causal_mask"]), 5, 9, ws.data_ptr() + ws_shift, n,
                          torch.cuda.current_stream().cuda_stream)
     assert rc == 0, fa._lib.strerror(rc)
     launches = fa.last_launch_count()
@@ -72,6 +74,23 @@ def test_both_routes_match_oracle(B, S_q, S_kv, D_qk, D_v, causal, p):
         for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
             assert rel(a, b) <= 1e-5, (route, name, rel(a, b))
     assert fa.device_status() == 0
+
+
+def test_gemm_route_with_a_64_byte_aligned_workspace():
+    rng = np.random.default_rng(64)
+    B, S_q, S_kv, D_qk, D_v = 2, 200, 264, 64, 64
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    do = rng.standard_normal((B, S_q, D_v)).astype(np.float32)
+    kw = dict(scale=0.125, dropout=0.1, causal_mask=False)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+    t = [torch.from_numpy(x).cuda() for x in (q, k, v, o_ref, s_ref, do)]
+    got, n = bwd(*t, kw, minimal=False, ws_shift=64)
+    assert n == 5
+    for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
+        assert rel(a, b) <= 1e-5, (name, rel(a, b))
 
 
 def test_workspace_query_sizes_the_gemm_route():

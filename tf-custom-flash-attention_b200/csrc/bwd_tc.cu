@@ -33,15 +33,14 @@ int launch_tc_bwd_t(const Params& p, cudaStream_t st, int* launches) {
   // dQ first: it also computes D = rowsum(dO * O) (into the workspace), which
   // the dK/dV kernel reads.
   sdpa_b200::record_bwd_event(0, st);
-  kq<<<static_cast<unsigned>(gq), tc::kBwdTcThreads, QCfg::kSmemBytes, st>>>(q128, do128, k128, v128, p);
+  if (int r = launch_tc(kq, gq, tc::kBwdTcThreads, QCfg::kSmemBytes, st, q128, do128, k128, v128, p)) return r;
   ++*launches;
-  if (int r = launch_result()) return r;
   sdpa_b200::record_bwd_event(1, st);
-  kkv<<<static_cast<unsigned>(gkv), tc::kBwdTcThreads, Cfg::kSmemBytes, st>>>(k128, v128, q64, do64, p);
+  if (int r = launch_tc(kkv, gkv, tc::kBwdTcThreads, Cfg::kSmemBytes, st, k128, v128, q64, do64, p)) return r;
   ++*launches;
   sdpa_b200::record_bwd_event(2, st);
   sdpa_b200::record_bwd_event(3, st);
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 // HEADS: [B/H, S, H, D] tensors (4-D TMA maps); else contiguous [B, S, D].

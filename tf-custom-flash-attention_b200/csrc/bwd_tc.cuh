@@ -101,6 +101,8 @@ __device__ __forceinline__ void bwd_setup(BwdBarriers* bars, uint32_t tmem_cols,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
+  pdl_wait();  // before any global access and before the wait deadline starts
 }
 
 // Producer of both kernels: the resident 128-row pair once, then n 64-row
@@ -569,6 +571,8 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
+  pdl_wait();  // before any global access and before the wait deadline starts
   const uint32_t tmem = bars->tmem_base;
   WaitCtl ctl;
   ctl.deadline_ns = globaltimer_ns() + p.timeout_ns;

@@ -23,10 +23,9 @@ int launch_tc_fwd_t(const Params& p, cudaStream_t st, int* launches) {
     return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
   const int64_t n_qt = (p.S_q + tc::kBM - 1) / tc::kBM;
   const int64_t grid = n_qt * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tc::kFwdThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
+  if (int r = launch_tc(kern, grid, tc::kFwdThreads, Cfg::kSmemBytes, st, mq, mk, mv, p)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 template <int DQK, int DV, bool HEADS>
@@ -52,10 +51,9 @@ int launch_pair_fwd_t(const Params& p, cudaStream_t st, int* launches) {
       !make_map_f16(&mv, p.v, p.B, p.H, p.S_kv, p.D_v, tc::kBN))
     return SDPA_B200_ECUDA;  // detail recorded by make_map_f16
   const int64_t grid = ((p.S_q + 2 * tc::kBM - 1) / (2 * tc::kBM)) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tc::kPairThreads, Cfg::kSmemBytes, st>>>(mq, mk, mv, p);
+  if (int r = launch_tc(kern, grid, tc::kPairThreads, Cfg::kSmemBytes, st, mq, mk, mv, p)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 template <int DQK, int DV>

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <utility>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -140,6 +142,35 @@ inline int num_sms() {
     cache[dev & 63].store(v);
   }
   return v;
+}
+
+// Launches a tensor-core kernel with programmatic stream serialisation: its
+// CTAs may start (and set up barriers and TMEM) while the previous kernel on
+// the stream finishes; the kernel waits (griddepcontrol.wait) before touching
+// global memory.  SDPA_B200_PDL=0 turns it off (plain stream order).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SDPA_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+inline int launch_tc(void (*kern)(KArgs...), int64_t grid, int threads, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  if (grid <= 0 || grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  return e == cudaSuccess ? SDPA_B200_OK : cuda_failure("kernel launch", e);
 }
 
 inline int launch_result() {

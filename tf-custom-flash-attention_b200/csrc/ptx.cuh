@@ -112,6 +112,18 @@ __device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* m, i
     tma_load_3d(dst, m, x, row, bo, bar);
 }
 
+// ------------------------------------------- programmatic dependent launch
+// With the launch attribute ProgrammaticStreamSerialization a kernel may start
+// while the previous kernel on the stream is still finishing; it must wait
+// here before touching global memory the previous kernel may read or write
+// (a no-op without the attribute).  Each tensor-core kernel calls both right
+// after its set-up (barrier init, TMEM alloc), so the set-up of the next
+// kernel's CTAs overlaps this kernel's tail.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

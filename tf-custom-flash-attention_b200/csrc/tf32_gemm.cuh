@@ -169,6 +169,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
+  pdl_wait();  // before any global access and before the wait deadline starts
   const uint32_t tmem = bars->tmem_base;
   WaitCtl ctl;
   ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;

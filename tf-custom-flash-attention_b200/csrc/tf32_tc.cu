@@ -22,10 +22,9 @@ int launch_fwd_t(const Params& p, cudaStream_t st, int* launches) {
       !make_map_f32_mn(&mv, p.v, p.B, p.H, p.S_kv, p.D_v, Cfg::kBN))
     return SDPA_B200_ECUDA;  // detail recorded by make_map
   const int64_t grid = ((p.S_q + tf32::kBM - 1) / tf32::kBM) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tf32::kFwdThreads, Cfg::kSmemBytes, st>>>(mk, mv, p);
+  if (int r = launch_tc(kern, grid, tf32::kFwdThreads, Cfg::kSmemBytes, st, mk, mv, p)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 template <int DQK, int DV>
@@ -52,10 +51,9 @@ int launch_bwd_mode(const Params& p, cudaStream_t st, int* launches) {
                                       : make_map_f32(&mb, rows_q ? p.v : p.d_o, p.B, p.H, S_str, p.D_v, Cfg::kN);
   if (!ok_a || !ok_b) return SDPA_B200_ECUDA;  // detail recorded by make_map
   const int64_t grid = (((rows_q ? p.S_q : p.S_kv) + 127) / 128) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tf32::kBwdThreads, Cfg::kSmemBytes, st>>>(ma, mb, p);
+  if (int r = launch_tc(kern, grid, tf32::kBwdThreads, Cfg::kSmemBytes, st, ma, mb, p)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 // DQ first: it writes D = rowsum(dO * O) (into the workspace), which DK reads.
@@ -101,9 +99,9 @@ int launch_gemm(const float* a, int64_t ld, const void* b_src, int d_b, float* c
   // static round-robin (measured).
   const int64_t items = ((M + 127) / 128) * p.B;
   const int64_t grid = (K + Cfg::kK - 1) / Cfg::kK >= 64 || items < num_sms() ? items : num_sms();
-  kern<<<static_cast<unsigned>(grid), tf32::kGemmThreads, Cfg::kSmemBytes, st>>>(ma, mb, g);
+  if (int r = launch_tc(kern, grid, tf32::kGemmThreads, Cfg::kSmemBytes, st, ma, mb, g)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 template <int DQK, int DV, bool DROP, bool HEADS>
@@ -117,10 +115,9 @@ int launch_scores(const Params& p, cudaStream_t st, int* launches) {
       !make_map_f32(&mo, p.d_o, p.B, p.H, p.S_q, p.D_v, Cfg::kN))
     return SDPA_B200_ECUDA;  // detail recorded by make_map
   const int64_t grid = ((p.S_kv + 127) / 128) * p.B;
-  if (grid > 0x7fffffffLL) return SDPA_B200_EINVAL;
-  kern<<<static_cast<unsigned>(grid), tf32::kScoreThreads, Cfg::kSmemBytes, st>>>(mq, mo, p);
+  if (int r = launch_tc(kern, grid, tf32::kScoreThreads, Cfg::kSmemBytes, st, mq, mo, p)) return r;
   ++*launches;
-  return launch_result();
+  return SDPA_B200_OK;
 }
 
 // The GEMM route (p.ws_ds / p.ws_p set): D, the score pass writing dS and
