@@ -33,7 +33,7 @@ def unfold(x, B, H):  # [B*H, S, D] -> [B, S, H, D]
     (torch.float16, 1, 5, 96, 96, 32, 32, False, 0.1),       # tcgen05 path, D = 32 (zero-filled to 64)
     (torch.float16, 1, 3, 64, 64, 12, 20, False, 0.1),       # SIMT path (rows not 16-byte multiples)
     (torch.float32, 2, 2, 70, 150, 64, 64, False, 0.05),     # fp32, 3xTF32 tensor-core path
-    (torch.float32, 1, 2, 96, 96, 100, 36, True, 0.1),       # fp32, D_qk > 64: 3xTF32 forward, SIMT backward
+    (torch.float32, 1, 2, 96, 96, 100, 36, True, 0.1),       # fp32, D_qk > 64: 3xTF32 forward, GEMM-route backward
     (torch.float32, 1, 2, 40, 40, 6, 10, False, 0.0),        # fp32 SIMT path
 ])
 def test_bshd_equals_folded_bitwise(dtype, B, H, S_q, S_kv, D_qk, D_v, causal, p):

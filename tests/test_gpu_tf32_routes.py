@@ -76,6 +76,30 @@ def test_both_routes_match_oracle(B, S_q, S_kv, D_qk, D_v, causal, p):
     assert fa.device_status() == 0
 
 
+@pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
+    (2, 192, 192, 128, 64, True, 0.1),
+    (1, 100, 300, 96, 20, False, 0.0),
+])
+def test_gemm_route_serves_d_qk_128(B, S_q, S_kv, D_qk, D_v, causal, p):
+    """D_qk = 128 with D_v <= 64 runs on the tensor cores only on the GEMM route
+    (the recomputing passes do not fit TMEM)."""
+    assert fa.kernel_path(torch.float32, D_qk, D_v, backward=True) == "tcgen05-3xtf32"
+    rng = np.random.default_rng(D_qk + S_kv)
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    do = rng.standard_normal((B, S_q, D_v)).astype(np.float32)
+    kw = dict(scale=D_qk ** -0.5, dropout=p, causal_mask=causal)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+    t = [torch.from_numpy(x).cuda() for x in (q, k, v, o_ref, s_ref, do)]
+    got, n = bwd(*t, kw, minimal=False)
+    assert n == 5
+    for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
+        assert rel(a, b) <= 1e-5, (name, rel(a, b))
+    assert fa.device_status() == 0
+
+
 def test_gemm_route_with_a_64_byte_aligned_workspace():
     rng = np.random.default_rng(64)
     B, S_q, S_kv, D_qk, D_v = 2, 200, 264, 64, 64
@@ -101,5 +125,6 @@ def test_workspace_query_sizes_the_gemm_route():
     full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 64, 128)
     assert full >= B * S_q * 4 + 2 * B * S_q * 72 * 4  # dS, P~: rows of S_kv padded to 16 bytes
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F16, B, S_q, S_kv, 64, 128) == B * S_q * 4
-    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) == B * S_q * 4
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) > B * S_q * 4  # D_qk = 128: GEMM route
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 128) == B * S_q * 4  # SIMT
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4

@@ -121,9 +121,13 @@ bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void*
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
 }
 
-bool tf32_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n) {
+// gemm: the workspace admits the GEMM route, which also serves D_qk = 128
+// with D_v <= 64 (the recomputing passes need D_qk <= 64).
+bool tf32_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n,
+                 bool gemm) {
   if (force_simt() || dtype != SDPA_B200_F32 || S_q == 0 || S_kv == 0) return false;
-  if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return false;
+  if (D_qk % 4 != 0 || D_v % 4 != 0) return false;
+  if (D_qk > 64 && !(gemm && D_v <= 64)) return false;
   for (int i = 0; i < n; ++i)
     if (!aligned16(ptrs[i])) return false;
   return true;
@@ -214,7 +218,7 @@ static size_t delta_bytes(int64_t B, int64_t S_q) {
 }
 static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
   if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
-  if (D_qk % 4 != 0 || D_v % 4 != 0 || D_qk > 64) return 0;
+  if (D_qk % 4 != 0 || D_v % 4 != 0 || (D_qk > 64 && D_v > 64)) return 0;
   const size_t one = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
   return 2 * one <= kGemmWorkspaceCap ? 2 * one + 256 : 0;  // + room to align the start to 256 bytes
 }
@@ -256,9 +260,10 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (int r = bind_context()) return r;
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
-  if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) {
-    const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
-    if (extra && workspace_bytes >= delta_bytes(B, S_q) + extra) {
+  const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
+  const bool gemm = extra && workspace_bytes >= delta_bytes(B, S_q) + extra;
+  if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8, gemm)) {
+    if (gemm) {
       const uintptr_t w0 = reinterpret_cast<uintptr_t>(workspace) + delta_bytes(B, S_q);
       uint8_t* w = reinterpret_cast<uint8_t*>((w0 + 255u) & ~uintptr_t(255u));
       p.ld_k = round_up(S_kv, 4);
@@ -346,10 +351,11 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
+  (void)backward;  // both directions cover the same shapes (see the header)
   if (force_simt()) return 0;
   if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0 && D_qk >= 16) ? 1 : 0;
-  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (backward ? D_qk <= 64 : (D_qk <= 64 || D_v <= 64)))
-    return 2;
+  // fp32 backward with D_qk = 128 (D_v <= 64): with the full workspace (GEMM route)
+  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (D_qk <= 64 || D_v <= 64)) return 2;
   return 0;
 }
 

@@ -164,6 +164,17 @@ int launch_bwd_d(const Params& p, cudaStream_t st, int* launches) {
                       : launch_bwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
+// D_qk = 128 (D_v <= 64): the GEMM route only (the recomputing passes do not
+// fit TMEM; the score pass holds K, V hi / lo in 2*128 + 2*64 columns).
+template <int DQK, int DV>
+int launch_bwd_gemm_d(const Params& p, cudaStream_t st, int* launches) {
+  if (p.H > 1)
+    return p.dropout_on ? launch_bwd_gemm_t<DQK, DV, true, true>(p, st, launches)
+                        : launch_bwd_gemm_t<DQK, DV, false, true>(p, st, launches);
+  return p.dropout_on ? launch_bwd_gemm_t<DQK, DV, true, false>(p, st, launches)
+                      : launch_bwd_gemm_t<DQK, DV, false, false>(p, st, launches);
+}
+
 }  // namespace
 
 // Not both D_qk and D_v over 64 (the caller checks; see FwdCfg).
@@ -179,9 +190,14 @@ int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) 
   return launch_fwd_d<64, 64>(p, st, launches);
 }
 
-// D_qk <= 64 only (the caller checks): with D_qk = 128 the resident operands
-// and accumulators of the DQ pass exceed TMEM.
+// D_qk <= 64 on either route; D_qk = 128 with D_v <= 64 on the GEMM route
+// only (the caller checks): with D_qk = 128 the resident operands and
+// accumulators of the DQ pass exceed TMEM.
 int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
+  if (p.D_qk > 64) {
+    if (!p.ws_ds || p.D_v > 64) return SDPA_B200_EUNSUPPORTED;
+    return p.D_v <= 32 ? launch_bwd_gemm_d<128, 32>(p, st, launches) : launch_bwd_gemm_d<128, 64>(p, st, launches);
+  }
   if (p.D_v > 64) return launch_bwd_d<64, 128>(p, st, launches);
   if (p.D_v <= 32) return launch_bwd_d<64, 32>(p, st, launches);
   return launch_bwd_d<64, 64>(p, st, launches);
