@@ -47,6 +47,9 @@ struct Params {
   float* ws_ds;
   float* ws_p;
   int64_t ld_k;
+  // fp32 forward: tiles per output fold segment, in units of the kernel's own
+  // segment (default 2; SDPA_B200_TF32_FOLD, a tuning knob)
+  int tf32_fold;
 };
 
 // CTA order of the tensor-core kernels over (batch row b, tile t): groups of

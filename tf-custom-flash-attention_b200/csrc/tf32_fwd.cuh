@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         const uint32_t tPh = tmem + Cfg::kS + (t & 1) * 2 * kBN, tPl = tPh + kBN;
         // a fresh accumulator at the first tile of each flush segment
-        const bool fresh = Cfg::kFlush ? (t % (Cfg::kFlush ? Cfg::kFlush : 1)) == 0 : t == 0;
+        const bool fresh = Cfg::kFlush ? (t % (Cfg::kFlush * p.tf32_fold)) == 0 : t == 0;
 #pragma unroll
         for (int kk = 0; kk < kBN / 8; ++kk) {
           const uint64_t vh = make_sw128_32b_desc(sb + Cfg::vhi(s) + kk * 1024, kBN * 128, 512);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // segment, and whenever the reference max moved (then O and the total
       // are rescaled by alpha and O restarts from zero).  s_full(j) implies
       // PV(j-2) completed, so o_done is at most one phase behind here.
-      const bool flush_now = Cfg::kFlush && j > 0 && (j % (Cfg::kFlush ? Cfg::kFlush : 1)) == 0;
+      const bool flush_now = Cfg::kFlush && j > 0 && (j % (Cfg::kFlush * p.tf32_fold)) == 0;
       if (flush_now || __any_sync(0xffffffffu, rescale_o)) {
         if (!tc::warp_wait(&bars->o_done, (j - 1) & 1, ctl)) {
           ok = false;

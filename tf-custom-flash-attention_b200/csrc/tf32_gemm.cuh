@@ -95,11 +95,6 @@ __device__ __forceinline__ void gemm_tmem_ld(uint32_t taddr, uint32_t* r) {
   }
 }
 
-// tm_a: 3-D map of the materialised matrix: K-major (A_MN false: K-dim
-// innermost, box 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN true: the
-// stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
-// atoms; dK and dV read dS and P~ this way).  tm_b: MN-major map of K, Q or dO, box 32
-// columns x 32 K-dim.
 // One work item = 128 result rows of one batch row: its K-dim tiles [tile0,
 // tile0 + n) (causal ranges) and its TMA coordinates.
 struct GemmItem {
@@ -186,6 +181,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int64_t item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
         const GemmItem it = gemm_item<HEADS>(g, item, kK);
         for (int t = 0; t < it.n; ++t, ++q) {
+          ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;  // per tile: a persistent CTA may run long
           const int s = q % kStages;
           GEMM_PROBE_T0(p0);
           if (!mbar_wait(&bars->st_empty[s], ((q / kStages) & 1) ^ 1, ctl)) {
@@ -225,6 +221,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t sb = smem_u32(smem);
       constexpr uint32_t idesc = make_idesc(128, N, false, true, true);  // A from TMEM
       for (int q = 0; q < n_tiles; ++q) {
+        ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;
         const int s = q % kStages, ab = q & 1;
         // accumulator ab was folded by the epilogue (its use q - 2)
         GEMM_PROBE_T0(w0);
@@ -265,6 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int tid = threadIdx.x - 256;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     for (int q = 0; q < n_tiles; ++q) {
+      ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;
       const int s = q % kStages;
       GEMM_PROBE_T0(c0);
       if (!tc::warp_wait(&bars->st_full[s], (q / kStages) & 1, ctl)) break;
@@ -320,6 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
     for (int e = 0; e < kHC; ++e) tot[e] = 0.0f;
     for (int qf = 0; qf < n_tiles; ++qf) {
+      ctl.deadline_ns = globaltimer_ns() + g.timeout_ns;
       const int ab = qf & 1;
       GEMM_PROBE_T0(e0);
       if (!tc::warp_wait(&bars->acc_full[ab], (qf >> 1) & 1, ctl)) break;

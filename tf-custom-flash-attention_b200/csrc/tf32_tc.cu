@@ -127,6 +127,7 @@ template <int DQK, int DV, bool DROP, bool HEADS>
 int launch_bwd_gemm_t(const Params& p, cudaStream_t st, int* launches) {
   sdpa_b200::record_bwd_event(0, st);
   const int64_t rows = p.B * p.S_q;
+  if ((rows + 7) / 8 > 0x7fffffffLL) return SDPA_B200_EINVAL;
   tf32::delta_kernel<HEADS><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(p);
   ++*launches;
   if (int r = launch_result()) return r;
