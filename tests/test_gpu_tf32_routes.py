@@ -128,3 +128,25 @@ def test_workspace_query_sizes_the_gemm_route():
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) > B * S_q * 4  # D_qk = 128: GEMM route
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 128) == B * S_q * 4  # SIMT
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4
+
+
+@pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
+    (1, 256, 4096, 128, 128, False, 0.05),
+    (2, 200, 200, 100, 72, True, 0.1),
+])
+def test_forward_with_both_dims_over_64(B, S_q, S_kv, D_qk, D_v, causal, p):
+    """The fp32 forward with D_qk and D_v over 64 keeps Q lo in shared memory
+    (TMEM holds Q hi, O, its running total and 32-key score tiles)."""
+    assert fa.kernel_path(torch.float32, D_qk, D_v) == "tcgen05-3xtf32"
+    rng = np.random.default_rng(D_v + S_kv)
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    kw = dict(scale=D_qk ** -0.5, dropout=p, causal_mask=causal)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    o, s = fa.sdpa(*[torch.from_numpy(x).cuda() for x in (q, k, v)], 5, 9, **kw)
+    assert fa.last_launch_count() == 1
+    torch.cuda.synchronize()
+    assert rel(o.cpu().numpy(), o_ref) <= 1e-5, rel(o.cpu().numpy(), o_ref)
+    assert rel(s.cpu().numpy(), s_ref) <= 1e-5, rel(s.cpu().numpy(), s_ref)
+    assert fa.device_status() == 0

@@ -118,14 +118,12 @@ bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, 
 }
 
 // fp32 on the 3xTF32 tensor-core kernels: rows must be 16-byte multiples
-// (TMA strides), every pointer 16-byte aligned; the backward serves D_qk <= 64.
+// (TMA strides), every pointer 16-byte aligned; the backward serves D_qk <= 64
+// (and D_qk = 128 with D_v <= 64 on the GEMM route).
 bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
                  const void* o) {
   if (force_simt() || dtype != SDPA_B200_F32 || S_kv == 0) return false;
   if (D_qk % 4 != 0 || D_v % 4 != 0) return false;
-  // With both over 64 the output has no TMEM room for a round-to-nearest
-  // running total and its error grows with S_kv past 1e-5: SIMT serves it.
-  if (D_qk > 64 && D_v > 64) return false;
   return aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
 }
 
@@ -362,11 +360,10 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
-  (void)backward;  // both directions cover the same shapes (see the header)
   if (force_simt()) return 0;
   if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0 && D_qk >= 16) ? 1 : 0;
   // fp32 backward with D_qk = 128 (D_v <= 64): with the full workspace (GEMM route)
-  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (D_qk <= 64 || D_v <= 64)) return 2;
+  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (!backward || D_qk <= 64 || D_v <= 64)) return 2;
   return 0;
 }
 

@@ -60,21 +60,27 @@ struct FwdCfg {
   // room, PV accumulates only kFlush tiles at a time (fresh accumulator at
   // every kFlush-th tile) and the softmax threads add each segment into a
   // running total OT (separate TMEM columns) in fp32 round-to-nearest.  With
-  // D_qk and D_v both over 64 there is no room (kFlush = 0); the library
-  // sends those shapes to the SIMT kernels.
+  // D_qk and D_v both over 64 that leaves no room for Q lo: it moves to shared
+  // memory (kQlSmem; the Q lo x K hi product becomes an SS MMA) and tiles are
+  // 32 keys.
   static constexpr bool kFits64 = 2 * DQK + 2 * DV + 4 * 64 <= 512;
   static constexpr bool kFits32 = 2 * DQK + 2 * DV + 4 * 32 <= 512;
+  static constexpr bool kQlSmem = !kFits32;
+  static_assert(!kQlSmem || DQK + 2 * DV + 4 * 32 <= 512, "TMEM budget with Q lo in shared memory");
   static constexpr int kBN = kFits64 ? 64 : 32;
-  static constexpr int kFlush = kFits64 ? 1 : (kFits32 ? 2 : 0);  // 0: never
+  static constexpr int kFlush = kFits64 ? 1 : 2;
   static constexpr uint32_t kKBytes = kBN * DQK * 4;  // one of hi / lo
   static constexpr uint32_t kVBytes = kBN * DV * 4;
   static constexpr uint32_t kStageBytes = 2 * (kKBytes + kVBytes);
-  static constexpr int kStages = 3 * kStageBytes <= 200 * 1024 ? 3 : 2;
-  static constexpr uint32_t kBarOff = kStages * kStageBytes;
+  static constexpr uint32_t kQlBytes = kQlSmem ? kBM * DQK * 4 : 0;  // K-major, 128-byte swizzle
+  static constexpr int kStages = 3 * kStageBytes + kQlBytes <= 200 * 1024 ? 3 : 2;
+  static constexpr uint32_t kQlOff = kStages * kStageBytes;
+  static constexpr uint32_t kBarOff = kQlOff + kQlBytes;
   static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
-  static constexpr uint32_t kQh = 0, kQl = DQK, kO = 2 * DQK;
-  static constexpr uint32_t kOT = 2 * DQK + DV;                       // running total (kFlush > 0)
-  static constexpr uint32_t kS = 2 * DQK + DV + (kFlush ? DV : 0);    // two buffers of 2 kBN columns
+  static constexpr uint32_t kQh = 0, kQl = DQK;                       // kQl: TMEM (unless kQlSmem)
+  static constexpr uint32_t kO = kQlSmem ? DQK : 2 * DQK;
+  static constexpr uint32_t kOT = kO + DV;                            // running total
+  static constexpr uint32_t kS = kOT + DV;                            // two buffers of 2 kBN columns
   static_assert(kS + 4 * kBN <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory");
   // stage s: K hi, K lo, V hi, V lo
@@ -138,6 +144,28 @@ __device__ __forceinline__ void row_to_tmem(const float* row, int c0, int ncols,
   }
   SDPA_TMEM_ST32(th, h);
   SDPA_TMEM_ST32(tl, l);
+}
+
+// row_to_tmem with the lo parts to a 128-byte shared-memory row (16-byte chunk
+// g at chunk g ^ sw) instead of TMEM.
+__device__ __forceinline__ void row_to_tmem_smem(const float* row, int c0, int ncols, bool valid, uint32_t th,
+                                                 uint8_t* lo_row, int sw) {
+  uint32_t h[32];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid && c0 + 4 * g < ncols) x = *reinterpret_cast<const float4*>(row + c0 + 4 * g);
+    const float xv[4] = {x.x, x.y, x.z, x.w};
+    float lv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float a;
+      split_tf32(xv[e], a, lv[e]);
+      h[4 * g + e] = __float_as_uint(a);
+    }
+    *reinterpret_cast<float4*>(lo_row + ((g ^ sw) << 4)) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+  }
+  SDPA_TMEM_ST32(th, h);
 }
 
 // Stores TMEM columns [0, 32*nchunks) of this lane (from taddr), times mul, to
@@ -276,7 +304,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const uint64_t bl = make_sw128_desc(sb + Cfg::klo(s) + off, 16, 1024);
           mma_tf32_ts(tS, tmem + Cfg::kQh + kk * 8, bh, idesc_s, kk > 0 ? 1u : 0u);
           mma_tf32_ts(tS, tmem + Cfg::kQh + kk * 8, bl, idesc_s, 1u);
-          mma_tf32_ts(tS, tmem + Cfg::kQl + kk * 8, bh, idesc_s, 1u);
+          if constexpr (Cfg::kQlSmem)  // Q lo from shared memory: box kk / 4, 32-byte step kk % 4
+            mma_tf32_ss(tS, make_sw128_desc(sb + Cfg::kQlOff + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024),
+                        bh, idesc_s, 1u);
+          else
+            mma_tf32_ts(tS, tmem + Cfg::kQl + kk * 8, bh, idesc_s, 1u);
         }
         mma_commit(&bars->s_full[j & 1]);
         TF32F_ADD(1, a1);
@@ -353,9 +385,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     {
       const float* qrow = static_cast<const float*>(p.q) + (row_ok ? row_offset_t<HEADS>(p.H, b, row, p.S_q, p.D_qk) : 0);
 #pragma unroll
-      for (int c = 0; c < DQK / 32; ++c)
-        row_to_tmem(qrow, c * 32, p.D_qk, row_ok, tmem + lane_base + Cfg::kQh + c * 32,
-                    tmem + lane_base + Cfg::kQl + c * 32);
+      for (int c = 0; c < DQK / 32; ++c) {
+        if constexpr (Cfg::kQlSmem)  // lo: row t of box c, 16-byte chunk g at g ^ (t & 7)
+          row_to_tmem_smem(qrow, c * 32, p.D_qk, row_ok, tmem + lane_base + Cfg::kQh + c * 32,
+                           smem + Cfg::kQlOff + c * (kBM * 128) + t * 128, t & 7);
+        else
+          row_to_tmem(qrow, c * 32, p.D_qk, row_ok, tmem + lane_base + Cfg::kQh + c * 32,
+                      tmem + lane_base + Cfg::kQl + c * 32);
+      }
+      if (Cfg::kQlSmem) fence_proxy_async_smem();
       if (Cfg::kFlush) {  // running output total starts at zero
         uint32_t z[32];
 #pragma unroll

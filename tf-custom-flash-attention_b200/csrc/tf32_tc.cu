@@ -178,10 +178,10 @@ int launch_bwd_gemm_d(const Params& p, cudaStream_t st, int* launches) {
 
 }  // namespace
 
-// Not both D_qk and D_v over 64 (the caller checks; see FwdCfg).
+// Every D_qk, D_v <= 128 (both over 64: Q lo in shared memory, see FwdCfg).
 int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) {
   const bool q128 = p.D_qk > 64, v128 = p.D_v > 64;
-  if (q128 && v128) return SDPA_B200_EUNSUPPORTED;
+  if (q128 && v128) return launch_fwd_d<128, 128>(p, st, launches);
   if (q128) return launch_fwd_d<128, 64>(p, st, launches);
   if (v128) return launch_fwd_d<64, 128>(p, st, launches);
 #ifndef SDPA_B200_TF32_NARROW_FWD
