@@ -127,10 +127,9 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream);
 
 /* Which kernel family serves a shape: 1 = fp16 tcgen05 tensor-core kernels,
  * 2 = fp32 3xTF32 tcgen05 kernels, 0 = SIMT kernels (rows that are not
- * 16-byte multiples, fp16 D_qk < 16, the fp32 backward with D_qk and D_v
- * both over 64, or forced by SDPA_B200_FORCE_SIMT=1).  For a backward given
- * the workspace sdpa_b200_bwd_workspace_bytes asks for (with less, the fp32
- * backward with D_qk > 64 runs on SIMT). */
+ * 16-byte multiples, fp16 D_qk < 16, or forced by SDPA_B200_FORCE_SIMT=1).
+ * For a backward given the workspace sdpa_b200_bwd_workspace_bytes asks for
+ * (with less, the fp32 backward with D_qk > 64 runs on SIMT). */
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward);
 
 /* Number of kernel launches the last successful fwd/bwd call on this thread made. */

@@ -44,7 +44,7 @@ def test_path_selection():
     assert fa.kernel_path(torch.float32, 32, 4, backward=True) == "tcgen05-3xtf32"
     assert fa.kernel_path(torch.float32, 128, 64) == "tcgen05-3xtf32"
     assert fa.kernel_path(torch.float32, 128, 128) == "tcgen05-3xtf32"  # Q lo in shared memory
-    assert fa.kernel_path(torch.float32, 128, 128, backward=True) == "simt"
+    assert fa.kernel_path(torch.float32, 128, 128, backward=True) == "tcgen05-3xtf32"  # GEMM route, V lo in smem
     assert fa.kernel_path(torch.float32, 128, 64, backward=True) == "tcgen05-3xtf32"  # GEMM route
     assert fa.kernel_path(torch.float32, 5, 3) == "simt"
 

@@ -79,10 +79,13 @@ def test_both_routes_match_oracle(B, S_q, S_kv, D_qk, D_v, causal, p):
 @pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
     (2, 192, 192, 128, 64, True, 0.1),
     (1, 100, 300, 96, 20, False, 0.0),
+    (1, 256, 1024, 128, 128, False, 0.05),
+    (2, 150, 150, 100, 88, True, 0.1),
 ])
 def test_gemm_route_serves_d_qk_128(B, S_q, S_kv, D_qk, D_v, causal, p):
-    """D_qk = 128 with D_v <= 64 runs on the tensor cores only on the GEMM route
-    (the recomputing passes do not fit TMEM)."""
+    """D_qk = 128 runs on the tensor cores only on the GEMM route (the
+    recomputing passes do not fit TMEM); with D_v over 64 as well the score
+    pass keeps V lo in shared memory."""
     assert fa.kernel_path(torch.float32, D_qk, D_v, backward=True) == "tcgen05-3xtf32"
     rng = np.random.default_rng(D_qk + S_kv)
     q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
@@ -118,15 +121,15 @@ def test_gemm_route_with_a_64_byte_aligned_workspace():
 
 
 def test_workspace_query_sizes_the_gemm_route():
-    """fp32 shapes the route serves ask for dS and P~; fp16 and shapes over
-    the cap ask for one float per query row."""
+    """fp32 shapes ask for dS and P~; fp16 and shapes over the cap ask for one
+    float per query row."""
     L = fa._lib.lib()
     B, S_q, S_kv = 2, 100, 70
     full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 64, 128)
     assert full >= B * S_q * 4 + 2 * B * S_q * 72 * 4  # dS, P~: rows of S_kv padded to 16 bytes
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F16, B, S_q, S_kv, 64, 128) == B * S_q * 4
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) > B * S_q * 4  # D_qk = 128: GEMM route
-    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 128) == B * S_q * 4  # SIMT
+    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 128) > B * S_q * 4
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4
 
 

@@ -119,7 +119,7 @@ bool tc_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, 
 
 // fp32 on the 3xTF32 tensor-core kernels: rows must be 16-byte multiples
 // (TMA strides), every pointer 16-byte aligned; the backward serves D_qk <= 64
-// (and D_qk = 128 with D_v <= 64 on the GEMM route).
+// (and D_qk = 128 on the GEMM route).
 bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* q, const void* k, const void* v,
                  const void* o) {
   if (force_simt() || dtype != SDPA_B200_F32 || S_kv == 0) return false;
@@ -128,12 +128,12 @@ bool tf32_fwd_ok(int dtype, int64_t S_kv, int64_t D_qk, int64_t D_v, const void*
 }
 
 // gemm: the workspace admits the GEMM route, which also serves D_qk = 128
-// with D_v <= 64 (the recomputing passes need D_qk <= 64).
+// (the recomputing passes need D_qk <= 64).
 bool tf32_bwd_ok(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v, const void* const* ptrs, int n,
                  bool gemm) {
   if (force_simt() || dtype != SDPA_B200_F32 || S_q == 0 || S_kv == 0) return false;
   if (D_qk % 4 != 0 || D_v % 4 != 0) return false;
-  if (D_qk > 64 && !(gemm && D_v <= 64)) return false;
+  if (D_qk > 64 && !gemm) return false;
   for (int i = 0; i < n; ++i)
     if (!aligned16(ptrs[i])) return false;
   return true;
@@ -224,7 +224,7 @@ static size_t delta_bytes(int64_t B, int64_t S_q) {
 }
 static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
   if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
-  if (D_qk % 4 != 0 || D_v % 4 != 0 || (D_qk > 64 && D_v > 64)) return 0;
+  if (D_qk % 4 != 0 || D_v % 4 != 0) return 0;
   // B * S_q * S_kv * 8 bytes over the cap (tested without overflowing int64)
   const int64_t ld = round_up(S_kv, 4), cap_elems = static_cast<int64_t>(kGemmWorkspaceCap / 8);
   if (S_q > cap_elems / ld || B > cap_elems / (S_q * ld)) return 0;
@@ -362,8 +362,9 @@ int sdpa_b200_test_wait_timeout(uint64_t timeout_ns, void* stream) {
 int sdpa_b200_path(int dtype, int64_t D_qk, int64_t D_v, int backward) {
   if (force_simt()) return 0;
   if (dtype == SDPA_B200_F16) return (D_qk % 8 == 0 && D_v % 8 == 0 && D_qk >= 16) ? 1 : 0;
-  // fp32 backward with D_qk = 128 (D_v <= 64): with the full workspace (GEMM route)
-  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0 && (!backward || D_qk <= 64 || D_v <= 64)) return 2;
+  // the fp32 backward with D_qk > 64 given the full workspace (GEMM route)
+  (void)backward;
+  if (dtype == SDPA_B200_F32 && D_qk % 4 == 0 && D_v % 4 == 0) return 2;
   return 0;
 }
 

@@ -43,10 +43,13 @@ constexpr int kScoreThreads = 448;
 
 template <int DQK, int DV>
 struct ScoreCfg {
-  // TMEM columns: K hi / lo, V hi / lo, then S^T (kN) and dP^T (kN)
-  static constexpr uint32_t kKh = 0, kKl = DQK, kVh = 2 * DQK, kVl = 2 * DQK + DV;
-  static constexpr uint32_t kT = 2 * DQK + 2 * DV;
-  static constexpr int kN = (512 - static_cast<int>(kT)) / 2 >= 64 ? 64 : 32;  // query rows per tile
+  // TMEM columns: K hi / lo, V hi / lo, then S^T (kN) and dP^T (kN).  With
+  // both D at 128 that leaves no room for a tile: V lo moves to shared memory
+  // (kVlSmem; its product with dO hi becomes an SS MMA) and tiles are 32 rows.
+  static constexpr bool kVlSmem = 2 * DQK + 2 * DV + 2 * 32 > 512;
+  static constexpr uint32_t kKh = 0, kKl = DQK, kVh = 2 * DQK, kVl = 2 * DQK + DV;  // kVl: TMEM (unless kVlSmem)
+  static constexpr uint32_t kT = 2 * DQK + (kVlSmem ? 1 : 2) * DV;
+  static constexpr int kN = !kVlSmem && (512 - static_cast<int>(kT)) / 2 >= 64 ? 64 : 32;  // query rows per tile
   static constexpr int kHalf = kN / 2;
   static_assert(kT + 2 * kN <= 512, "TMEM budget");
   // shared memory per stage: Q hi, Q lo (kN x DQK), dO hi, dO lo (kN x DV),
@@ -57,9 +60,11 @@ struct ScoreCfg {
   static constexpr uint32_t kQBytes = kN * DQK * 4, kOBytes = kN * DV * 4;
   static constexpr uint32_t kStageBytes = 2 * kQBytes + 2 * kOBytes;
   static constexpr uint32_t kStageAligned = (kStageBytes + 1023) / 1024 * 1024;
-  static constexpr int kStages = 3 * kStageAligned <= 200 * 1024 ? 3 : 2;
+  static constexpr uint32_t kVlBytes = kVlSmem ? 128 * DV * 4 : 0;  // K-major, 128-byte swizzle
+  static constexpr int kStages = 3 * kStageAligned + kVlBytes <= 200 * 1024 ? 3 : 2;
   static constexpr int kVecSlots = 4;
-  static constexpr uint32_t kVecOff = kStages * kStageAligned;
+  static constexpr uint32_t kVlOff = kStages * kStageAligned;
+  static constexpr uint32_t kVecOff = kVlOff + kVlBytes;
   static constexpr uint32_t kBarOff = kVecOff + kVecSlots * 2 * kN * 4;
   static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -79,6 +84,24 @@ struct ScoreBarriers {
   uint32_t tmem_base;
   int abort_flag;
 };
+
+// issue_scores (tf32_bwd.cuh) with the A lo operand in shared memory (128
+// rows, K-major, 128-byte swizzle, boxes of 32 columns): out = A B^T.
+template <int D, int kN>
+__device__ __forceinline__ void issue_scores_lo_smem(uint32_t out, uint32_t ah, uint32_t al_smem, uint32_t bh,
+                                                     uint32_t bl) {
+  constexpr uint32_t idesc = make_idesc(128, kN, false, false, true);
+#pragma unroll
+  for (int kk = 0; kk < D / 8; ++kk) {
+    const uint32_t off = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
+    const uint64_t dh = make_sw128_desc(bh + off, 16, 1024);
+    const uint64_t dl = make_sw128_desc(bl + off, 16, 1024);
+    const uint64_t da = make_sw128_desc(al_smem + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024);
+    mma_tf32_ts(out, ah + kk * 8, dh, idesc, kk > 0 ? 1u : 0u);
+    mma_tf32_ts(out, ah + kk * 8, dl, idesc, 1u);
+    mma_tf32_ss(out, da, dh, idesc, 1u);
+  }
+}
 
 // tm_q: Q [B/H, S_q, H, D_qk], tm_o: dO [B/H, S_q, H, D_v], both box 32 x kN.
 template <int DQK, int DV, bool DROP, bool HEADS>
@@ -178,7 +201,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         SCORE_PROBE_T0(w2);
         tc_fence_after();
         issue_scores<DQK, kN>(tT, tmem + Cfg::kKh, tmem + Cfg::kKl, sb + Cfg::q_hi(s), sb + Cfg::q_lo(s));
-        issue_scores<DV, kN>(tT + kN, tmem + Cfg::kVh, tmem + Cfg::kVl, sb + Cfg::o_hi(s), sb + Cfg::o_lo(s));
+        if constexpr (Cfg::kVlSmem)
+          issue_scores_lo_smem<DV, kN>(tT + kN, tmem + Cfg::kVh, sb + Cfg::kVlOff, sb + Cfg::o_hi(s), sb + Cfg::o_lo(s));
+        else
+          issue_scores<DV, kN>(tT + kN, tmem + Cfg::kVh, tmem + Cfg::kVl, sb + Cfg::o_hi(s), sb + Cfg::o_lo(s));
         mma_commit(&bars->s_full);
         mma_commit(&bars->st_empty[s]);
         SCORE_PROBE_ADD(2, w2);
@@ -237,9 +263,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 #pragma unroll
         for (int c = 0; c < HC / 32; ++c) {
           const int cc = half * HC + c * 32;
-          row_to_tmem(vrow, cc, p.D_v, row_ok, tmem + lane_base + Cfg::kVh + cc, tmem + lane_base + Cfg::kVl + cc);
+          if constexpr (Cfg::kVlSmem)  // lo: row r of box cc / 32, 16-byte chunk g at g ^ (r & 7)
+            row_to_tmem_smem(vrow, cc, p.D_v, row_ok, tmem + lane_base + Cfg::kVh + cc,
+                             smem + Cfg::kVlOff + (cc / 32) * (128 * 128) + r * 128, r & 7);
+          else
+            row_to_tmem(vrow, cc, p.D_v, row_ok, tmem + lane_base + Cfg::kVh + cc, tmem + lane_base + Cfg::kVl + cc);
         }
       }
+      if (Cfg::kVlSmem) fence_proxy_async_smem();
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->res_ready);

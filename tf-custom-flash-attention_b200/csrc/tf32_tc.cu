@@ -165,8 +165,9 @@ int launch_bwd_d(const Params& p, cudaStream_t st, int* launches) {
                       : launch_bwd_t<DQK, DV, false, false>(p, st, launches);
 }
 
-// D_qk = 128 (D_v <= 64): the GEMM route only (the recomputing passes do not
-// fit TMEM; the score pass holds K, V hi / lo in 2*128 + 2*64 columns).
+// D_qk = 128: the GEMM route only (the recomputing passes do not fit TMEM;
+// the score pass holds K, V hi / lo in 2*128 + 2*64 columns, or with D_v =
+// 128 keeps V lo in shared memory).
 template <int DQK, int DV>
 int launch_bwd_gemm_d(const Params& p, cudaStream_t st, int* launches) {
   if (p.H > 1)
@@ -191,12 +192,13 @@ int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) 
   return launch_fwd_d<64, 64>(p, st, launches);
 }
 
-// D_qk <= 64 on either route; D_qk = 128 with D_v <= 64 on the GEMM route
-// only (the caller checks): with D_qk = 128 the resident operands and
-// accumulators of the DQ pass exceed TMEM.
+// D_qk <= 64 on either route; D_qk = 128 on the GEMM route only (the caller
+// checks): with D_qk = 128 the resident operands and accumulators of the DQ
+// pass exceed TMEM.
 int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
   if (p.D_qk > 64) {
-    if (!p.ws_ds || p.D_v > 64) return SDPA_B200_EUNSUPPORTED;
+    if (!p.ws_ds) return SDPA_B200_EUNSUPPORTED;
+    if (p.D_v > 64) return launch_bwd_gemm_d<128, 128>(p, st, launches);  // V lo in shared memory
     return p.D_v <= 32 ? launch_bwd_gemm_d<128, 32>(p, st, launches) : launch_bwd_gemm_d<128, 64>(p, st, launches);
   }
   if (p.D_v > 64) return launch_bwd_d<64, 128>(p, st, launches);
