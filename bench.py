@@ -450,12 +450,16 @@ def run_ours(args, w):
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
     d2h = 0
 
+    # about 16 MB of inputs per chunk (at most 16 chunks): a small step is not
+    # cut into launches shorter than their overhead
+    e2e_chunks = max(1, min(16, B, h2d // (16 << 20)))
+
     def e2e_step():
         # public host-buffer API: batch chunks pipelined over copy-in / compute / copy-out streams
         nonlocal outs_h, d2h
         outs_h = fa.pipeline.train_step_host(hq, hk, hv, hdo, w["seed"], offset, scale=kw["scale"],
                                              dropout=kw["dropout"], causal_mask=kw["causal_mask"],
-                                             chunks=min(16, B), device=dev, out=outs_h)
+                                             chunks=e2e_chunks, device=dev, out=outs_h)
         d2h = sum(x.numel() * x.element_size() for x in outs_h)
 
     e2e_steps = max(1, min(args.steps, 5))
@@ -544,7 +548,7 @@ def run_ours(args, w):
         "memory": {"min_bytes_per_step": mb, "achieved_gbs": mb / (ms * 1e-3) / 1e9, "peak_gbs": hbm[0],
                    "peak_kind": hbm[1], "frac": mb / (ms * 1e-3) / 1e9 / hbm[0]},
         "e2e": {"value": (f_fwd + f_bwd) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "chunks": e2e_chunks,
                 "bound": "pinned host<->device copies (see per_rank copy GB/s)"},
         "validated": validated, "validation": {"rows_checked": starts, "mismatches": mismatched,
                                                "method": "NCCL all_gather of each shard's first row; rank 0 "
