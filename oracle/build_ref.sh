@@ -4,8 +4,9 @@
 #   libsdpa_ref_cpu.so  sdpa/sdpa_cpu.cc (CPU OpKernels + CPU functors)
 #   libsdpa_ref_gpu.so  the same plus sdpa/sdpa_fwd.cu.cc and sdpa/sdpa_bwd.cu.cc
 #                       compiled for sm_100a (the reference's GPU op)
-# Test infrastructure only.  Needs the reference checkout (REF_DIR, default
-# /root/reference); on a machine without it the prebuilt oracle/_ref/*.so are used.
+# Test infrastructure only.  Needs the reference checkout (REF_DIR; its
+# default is set below); on a machine without it the prebuilt oracle/_ref/*.so
+# are used.
 # Flags follow the reference's build.sh: -O2, -march=native for the host code
 # (here -march=x86-64-v3 so the library also runs on the GPU box's host CPU).
 set -euo pipefail
