@@ -153,3 +153,26 @@ def test_forward_with_both_dims_over_64(B, S_q, S_kv, D_qk, D_v, causal, p):
     assert rel(o.cpu().numpy(), o_ref) <= 1e-5, rel(o.cpu().numpy(), o_ref)
     assert rel(s.cpu().numpy(), s_ref) <= 1e-5, rel(s.cpu().numpy(), s_ref)
     assert fa.device_status() == 0
+
+
+@pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
+    (128, 64, 384, 32, 32, False, 0.1),
+    (96, 256, 256, 64, 48, True, 0.0),
+])
+def test_persistent_gemms_over_many_items(B, S_q, S_kv, D_qk, D_v, causal, p):
+    """More work items than SMs: each persistent dK / dV GEMM CTA runs several
+    items back to back (item boundaries inside one pipeline)."""
+    rng = np.random.default_rng(B + S_kv)
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    do = rng.standard_normal((B, S_q, D_v)).astype(np.float32)
+    kw = dict(scale=D_qk ** -0.5, dropout=p, causal_mask=causal)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+    t = [torch.from_numpy(x).cuda() for x in (q, k, v, o_ref, s_ref, do)]
+    got, n = bwd(*t, kw, minimal=False)
+    assert n == 5
+    for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
+        assert rel(a, b) <= 1e-5, (name, rel(a, b))
+    assert fa.device_status() == 0
