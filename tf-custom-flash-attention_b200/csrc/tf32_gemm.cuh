@@ -14,10 +14,10 @@
 // only fit N = 32 tiles in TMEM, where a tf32 MMA runs at half its rate.
 //
 // A work item = 128 rows of the result, all N columns; persistent CTAs take
-// items in turn (below).  Streams K-dim tiles of 32:
+// items in turn (below).  Streams K-dim tiles of kK = 64 (32 at N = 128):
 // the A tile (128 x 32) and the B tile (32 x N, MN-major, 32-byte swizzle
 // atoms) by TMA.  Four converter warps split A row by row into tf32 hi / lo
-// in TMEM and B in place in shared memory; one thread issues 4 x 3 TS MMAs
+// in TMEM and B in place in shared memory; one thread issues kK / 8 x 3 TS MMAs
 // per tile (A from TMEM: only B is read from shared memory, whose bandwidth
 // bounded the all-shared-memory form) into one of two TMEM accumulators,
 // which 8 epilogue warps fold into an fp32 running total every tile (the
@@ -57,19 +57,31 @@ struct GemmArgs {
   uint64_t timeout_ns;
 };
 
+#ifndef SDPA_B200_GEMM_K
+#define SDPA_B200_GEMM_K 64
+#endif
 template <int N>
 struct GemmCfg {
-  static constexpr int kK = 32;                          // K-dim per tile (one 128-byte row)
-  static constexpr uint32_t kABytes = 128 * kK * 4;      // 16 KB
-  static constexpr uint32_t kBBytes = kK * N * 4;        // N / 32 boxes of 32 x 32
+  // K-dim per tile (kK / 32 boxes of 128-byte rows): 64 halves the per-tile
+  // hand-offs (cfg5 dQ 0.43 -> 0.37 ms, dK 0.39 -> 0.34); at N = 128 it
+  // leaves TMEM and shared memory two stages only, and 32 with four measured
+  // as fast (dV 0.51 / 0.52 ms)
+  static constexpr int kK = N >= 128 ? 32 : SDPA_B200_GEMM_K;
+  static_assert(kK == 32 || kK == 64, "K tile");
+  static constexpr uint32_t kABytes = 128 * kK * 4;      // 16 or 32 KB
+  static constexpr uint32_t kBBytes = kK * N * 4;        // N / 32 boxes of 32 columns x kK
   static constexpr uint32_t kStageBytes = kABytes + 2 * kBBytes;  // raw A, B hi, B lo
-  static constexpr int kStages = 4 * kStageBytes <= 200 * 1024 ? 4 : 3;
-  static constexpr uint32_t kBarOff = kStages * kStageBytes;
-  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
-  // TMEM: two accumulators (N columns each), then per stage A hi, A lo (32 each)
+  // TMEM: two accumulators (N columns each), then per stage A hi, A lo (kK each)
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kAslot0 = 2 * N;
-  static_assert(kAslot0 + kStages * 64 <= kTmemCols, "TMEM budget");
+  static constexpr int kSmemStages = 200 * 1024 / kStageBytes;
+  static constexpr int kTmemStages = (512 - 2 * N) / (2 * kK);
+  static constexpr int kStages = kSmemStages < kTmemStages ? (kSmemStages < 4 ? kSmemStages : 4)
+                                                           : (kTmemStages < 4 ? kTmemStages : 4);
+  static_assert(kStages >= 2, "pipeline depth");
+  static constexpr uint32_t kBarOff = kStages * kStageBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
+  static_assert(kAslot0 + kStages * 2 * kK <= kTmemCols, "TMEM budget");
   static constexpr int kHC = N / 2;                      // columns per epilogue thread
   static_assert(N == 32 || N == 64 || N == 128, "N");
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -129,10 +141,10 @@ __device__ __forceinline__ GemmItem gemm_item(const GemmArgs& g, int64_t item, i
 // does not pay the pipeline's fill and drain, and the epilogue of one item
 // overlaps the next item's loads and MMAs.
 // tm_a: 3-D map of the materialised matrix: K-major (A_MN false: K-dim
-// innermost, box 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN true: the
-// stored matrix is A^T, rows innermost, box 32 rows x 32 K-dim with 32-byte
+// innermost, kK / 32 boxes of 32 x 128 rows, 128-byte swizzle) or MN-major (A_MN
+// true: the stored matrix is A^T, rows innermost, boxes of 32 rows x kK K-dim with 32-byte
 // atoms; dK and dV read dS and P~ this way).  tm_b: MN-major map of K, Q or
-// dO, box 32 columns x 32 K-dim.
+// dO, box 32 columns x kK K-dim.
 template <int N, bool HEADS, bool A_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
@@ -197,8 +209,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tma_load_3d(smem + Cfg::a_raw(s) + c * kK * 128, &tm_a, static_cast<int>(it.m0) + c * 32, k0,
                           static_cast<int>(it.b), &bars->st_full[s]);
           } else {
-            tma_load_3d(smem + Cfg::a_raw(s), &tm_a, k0, static_cast<int>(it.m0), static_cast<int>(it.b),
-                        &bars->st_full[s]);
+#pragma unroll
+            for (int c = 0; c < kK / 32; ++c)
+              tma_load_3d(smem + Cfg::a_raw(s) + c * (128 * 128), &tm_a, k0 + c * 32, static_cast<int>(it.m0),
+                          static_cast<int>(it.b), &bars->st_full[s]);
           }
 #pragma unroll
           for (int c = 0; c < N / 32; ++c)
@@ -233,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         GEMM_PROBE_T0(w2);
         tc_fence_after();
         const uint32_t acc = tmem + ab * N;
-        const uint32_t ah = tmem + Cfg::kAslot0 + s * 64, al = ah + 32;
+        const uint32_t ah = tmem + Cfg::kAslot0 + s * 2 * kK, al = ah + kK;
 #pragma unroll
         for (int kk = 0; kk < kK / 8; ++kk) {
           const uint64_t bh = make_sw128_32b_desc(sb + Cfg::b_hi(s) + kk * 1024, kK * 128, 512);
@@ -268,35 +282,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!tc::warp_wait(&bars->st_full[s], (q / kStages) & 1, ctl)) break;
       if (tid == 0) GEMM_PROBE_ADD(6, c0);
       GEMM_PROBE_T0(c1);
-      uint32_t h[32], l[32];
       const uint8_t* a = smem + Cfg::a_raw(s);
-      if (A_MN) {  // box tid / 32, element tid % 32 of each 128-byte K row (32-byte atoms, XOR row & 3)
-        const uint8_t* box = a + (tid >> 5) * (kK * 128) + ((lane & 7) << 2);
+      const uint32_t ta = tmem + lane_base + Cfg::kAslot0 + s * 2 * kK;
 #pragma unroll
-        for (int k = 0; k < kK; ++k) {
-          float hi, lo;
-          split_tf32(*reinterpret_cast<const float*>(box + k * 128 + (((lane >> 3) ^ (k & 3)) << 5)), hi, lo);
-          h[k] = __float_as_uint(hi);
-          l[k] = __float_as_uint(lo);
-        }
-      } else {  // row tid: 16-byte chunk j at chunk j ^ (row & 7) (128-byte swizzle)
-        const uint8_t* row = a + tid * 128;
+      for (int kh = 0; kh < kK / 32; ++kh) {  // 32 K-dim values of the row at a time
+        uint32_t h[32], l[32];
+        if (A_MN) {  // box tid / 32, element tid % 32 of each 128-byte K row (32-byte atoms, XOR row & 3)
+          const uint8_t* box = a + (tid >> 5) * (kK * 128) + ((lane & 7) << 2);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (tid & 7)) << 4));
-          const float xv[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int k0 = 0; k0 < 32; ++k0) {
+            const int k = kh * 32 + k0;
             float hi, lo;
-            split_tf32(xv[e], hi, lo);
-            h[4 * j + e] = __float_as_uint(hi);
-            l[4 * j + e] = __float_as_uint(lo);
+            split_tf32(*reinterpret_cast<const float*>(box + k * 128 + (((lane >> 3) ^ (k & 3)) << 5)), hi, lo);
+            h[k0] = __float_as_uint(hi);
+            l[k0] = __float_as_uint(lo);
+          }
+        } else {  // box kh, row tid: 16-byte chunk j at chunk j ^ (row & 7) (128-byte swizzle)
+          const uint8_t* row = a + kh * (128 * 128) + tid * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (tid & 7)) << 4));
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float hi, lo;
+              split_tf32(xv[e], hi, lo);
+              h[4 * j + e] = __float_as_uint(hi);
+              l[4 * j + e] = __float_as_uint(lo);
+            }
           }
         }
+        SDPA_TMEM_ST32(ta + kh * 32, h);
+        SDPA_TMEM_ST32(ta + kK + kh * 32, l);
       }
-      const uint32_t ta = tmem + lane_base + Cfg::kAslot0 + s * 64;
-      SDPA_TMEM_ST32(ta, h);
-      SDPA_TMEM_ST32(ta + 32, l);
       split_tile(smem + Cfg::b_hi(s), smem + Cfg::b_lo(s), Cfg::kBBytes, tid, 128);
       tmem_wait_st();
       fence_proxy_async_smem();
