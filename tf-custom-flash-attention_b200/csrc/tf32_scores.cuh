@@ -10,8 +10,9 @@
 // elementwise formulas, skip rule (p <= 1e-6) and dropout counters are the
 // reference's dK/dV kernel's (sdpa/sdpa_bwd.cu.cc:125-170), as in the passes
 // of tf32_bwd.cuh.  Without an accumulator or dS operand in TMEM, the tile is
-// 64 query rows wide (against 32 in the recomputing DK pass): half as many
-// MMA instructions per score, each at a better rate.  The elementwise warps
+// 64 query rows wide (against 32 in the recomputing DK pass; 32 again with
+// both D at 128): half as many MMA instructions per score, each at a better
+// rate.  The elementwise warps
 // read S^T / dP^T into registers and release the buffer at once, so the next
 // tile's MMAs run under this tile's elementwise work.
 //
