@@ -57,9 +57,11 @@ int sdpa_b200_fwd(int dtype, const void* q, const void* k, const void* v, void* 
 
 /* Scratch the backward asks for (the caller allocates it; TF: allocate_temp):
  * one float32 per query row (rowsum(dO*O)), which is also the minimum
- * sdpa_b200_bwd accepts; for fp32 shapes on the tensor-core path (D_qk <= 64)
- * also room for dS and (dropout-scaled P)^T, about 4*B*S_q*S_kv bytes each,
- * up to 4 GiB in all, which selects the faster GEMM route of the backward. */
+ * sdpa_b200_bwd accepts; for fp32 (rows of 16-byte multiples) also room for
+ * dS and the dropout-scaled P, about 4*B*S_q*S_kv bytes each, which selects
+ * the faster GEMM route of the backward.  That part is capped at 4 GiB: past
+ * it the query asks for the batch rows that fit, and the backward runs in
+ * chunks of that many rows (of as many as any workspace given holds). */
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v);
 
 /* Backward: dq, dk, dv shaped like q, k, v (dtype), from q, k, v, out, stats

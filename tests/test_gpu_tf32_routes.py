@@ -121,8 +121,8 @@ def test_gemm_route_with_a_64_byte_aligned_workspace():
 
 
 def test_workspace_query_sizes_the_gemm_route():
-    """fp32 shapes ask for dS and P~; fp16 and shapes over the cap ask for one
-    float per query row."""
+    """fp32 shapes ask for dS and P~ (of every row, or of the rows that fit
+    under the cap); fp16 asks for one float per query row."""
     L = fa._lib.lib()
     B, S_q, S_kv = 2, 100, 70
     full = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 64, 128)
@@ -130,7 +130,8 @@ def test_workspace_query_sizes_the_gemm_route():
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F16, B, S_q, S_kv, 64, 128) == B * S_q * 4
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 64) > B * S_q * 4  # D_qk = 128: GEMM route
     assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, 128, 128) > B * S_q * 4
-    assert L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64) == 64 * 8192 * 4
+    big = L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, 64, 8192, 8192, 64, 64)  # 34 GB for all rows
+    assert 64 * 8192 * 4 + (2 << 30) < big <= 64 * 8192 * 4 + 4096 + (4 << 30)  # rows that fit under 4 GiB
 
 
 @pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p", [
@@ -176,3 +177,72 @@ def test_persistent_gemms_over_many_items(B, S_q, S_kv, D_qk, D_v, causal, p):
     for name, a, b in zip(("dq", "dk", "dv"), got, g_ref):
         assert rel(a, b) <= 1e-5, (name, rel(a, b))
     assert fa.device_status() == 0
+
+
+def _chunk_ws_bytes(B, S_q, S_kv, rows):
+    """Workspace for the delta rows of all B rows plus dS / P~ of `rows` rows."""
+    r256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    ld = (S_kv + 3) // 4 * 4
+    return r256(B * S_q * 4) + 2 * r256(rows * S_q * ld * 4) + 256
+
+
+@pytest.mark.parametrize("B,S_q,S_kv,D_qk,D_v,causal,p,rows", [
+    (5, 130, 130, 64, 128, True, 0.1, 2),
+    (3, 96, 200, 128, 64, False, 0.2, 1),
+])
+def test_gemm_route_in_batch_chunks(B, S_q, S_kv, D_qk, D_v, causal, p, rows):
+    """A workspace for fewer rows than the batch (as past the 4 GiB cap): the
+    GEMM route runs in chunks of that many rows, each with its rows' offsets
+    and dropout counters."""
+    rng = np.random.default_rng(B * 7 + rows)
+    q = (rng.standard_normal((B, S_q, D_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, S_kv, D_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, S_kv, D_v)) * 0.5).astype(np.float32)
+    do = rng.standard_normal((B, S_q, D_v)).astype(np.float32)
+    kw = dict(scale=D_qk ** -0.5, dropout=p, causal_mask=causal)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+    tq, tk, tv, to, ts, tdo = (torch.from_numpy(x).cuda() for x in (q, k, v, o_ref, s_ref, do))
+    L = fa._lib.lib()
+    n = _chunk_ws_bytes(B, S_q, S_kv, rows)
+    ws = torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+    dq, dk, dv = torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv)
+    rc = L.sdpa_b200_bwd(fa._lib.F32, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), to.data_ptr(), ts.data_ptr(),
+                         tdo.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q, S_kv, D_qk, D_v,
+                         kw["scale"], p, int(causal), 5, 9, ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, fa._lib.strerror(rc)
+    assert fa.last_launch_count() == 5 * ((B + rows - 1) // rows)
+    torch.cuda.synchronize()
+    for name, a, b in zip(("dq", "dk", "dv"), (dq, dk, dv), g_ref):
+        assert rel(a.cpu().numpy(), b) <= 1e-5, (name, rel(a.cpu().numpy(), b))
+    assert fa.device_status() == 0
+
+
+def test_gemm_route_in_batch_chunks_bshd():
+    """[B, S, H, D] layout: chunks hold whole outer batch rows (a multiple of H
+    folded rows); a workspace for 3 folded rows with H = 2 runs chunks of 2."""
+    B, H, S, D = 3, 2, 96, 64
+    rng = np.random.default_rng(11)
+    q, k, v, do = ((rng.standard_normal((B * H, S, D)) * 0.5).astype(np.float32) for _ in range(4))
+    kw = dict(scale=D ** -0.5, dropout=0.1, causal_mask=True)
+    o_ref, s_ref = cpu.sdpa(q, k, v, 5, 9, **kw)
+    g_ref = cpu.sdpa_grad(q, k, v, o_ref, s_ref, do, 5, 9, **kw)
+
+    def bshd(x):  # folded row b*H + h -> [B, S, H, D]
+        return torch.from_numpy(x).cuda().reshape(B, H, S, x.shape[2]).permute(0, 2, 1, 3).contiguous()
+
+    tq, tk, tv, to, tdo = (bshd(x) for x in (q, k, v, o_ref, do))
+    ts = torch.from_numpy(s_ref).cuda().reshape(B, H, S).contiguous()
+    L = fa._lib.lib()
+    n = _chunk_ws_bytes(B * H, S, S, 3)
+    ws = torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+    dq, dk, dv = torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv)
+    rc = L.sdpa_b200_bwd_bshd(fa._lib.F32, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), to.data_ptr(), ts.data_ptr(),
+                              None, tdo.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, H, S, S, D, D,
+                              kw["scale"], 0.1, 1, 5, 9, ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, fa._lib.strerror(rc)
+    assert fa.last_launch_count() == 5 * 3  # chunks of 2 folded rows
+    torch.cuda.synchronize()
+    for name, a, b in zip(("dq", "dk", "dv"), (dq, dk, dv), g_ref):
+        got = a.permute(0, 2, 1, 3).reshape(B * H, S, D).cpu().numpy()
+        assert rel(got, b) <= 1e-5, (name, rel(got, b))

@@ -213,23 +213,37 @@ int sdpa_b200_fwd_bshd(int dtype, const void* q, const void* k, const void* v, v
 }
 
 // Workspace of the fp32 backward's GEMM route beyond the delta rows: dS and
-// P~, [B, S_q, ld_k] each (ld_k = S_kv rounded up to 16 bytes), or 0 where
-// the route does not apply.  Capped so that
-// the workspace stays a small part of HBM; above the cap (and with a smaller
-// workspace) the three recomputing passes run instead.
+// P~, [rows, S_q, ld_k] each (ld_k = S_kv rounded up to 16 bytes).  The
+// query asks for all B rows up to a cap that keeps the workspace a small part
+// of HBM; past it, for as many rows as fit, and the backward runs in batch
+// chunks of that many rows.  Where not even one row fits (or the caller gives
+// less than one row's worth) the three recomputing passes run instead.
 constexpr size_t kGemmWorkspaceCap = size_t(4) << 30;
 static int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 static size_t delta_bytes(int64_t B, int64_t S_q) {
   return static_cast<size_t>(round_up(B * S_q * static_cast<int64_t>(sizeof(float)), 256));
 }
+static bool gemm_shape(int dtype, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
+  return !force_simt() && dtype == SDPA_B200_F32 && S_q > 0 && S_kv > 0 && D_qk % 4 == 0 && D_v % 4 == 0;
+}
+// bytes for `rows` batch rows (+ room to align the start to 256 bytes)
+static size_t gemm_chunk_bytes(int64_t rows, int64_t S_q, int64_t S_kv) {
+  return 2 * static_cast<size_t>(round_up(rows * S_q * round_up(S_kv, 4) * 4, 256)) + 256;
+}
+// most batch rows (<= B) whose chunk fits in `avail` bytes; 0 if none
+static int64_t gemm_rows_fitting(size_t avail, int64_t B, int64_t S_q, int64_t S_kv) {
+  const int64_t ld = round_up(S_kv, 4);
+  if (avail < 1024 || S_q > static_cast<int64_t>(avail / 8) / ld) return 0;  // not even one row
+  const int64_t row_bytes = 8 * S_q * ld;  // dS + P~ of one row
+  int64_t rows = static_cast<int64_t>(avail / static_cast<size_t>(row_bytes));
+  if (rows > B) rows = B;
+  while (rows > 0 && gemm_chunk_bytes(rows, S_q, S_kv) > avail) --rows;
+  return rows;
+}
 static size_t gemm_ws_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
-  if (force_simt() || dtype != SDPA_B200_F32 || B <= 0 || S_q <= 0 || S_kv <= 0) return 0;
-  if (D_qk % 4 != 0 || D_v % 4 != 0) return 0;
-  // B * S_q * S_kv * 8 bytes over the cap (tested without overflowing int64)
-  const int64_t ld = round_up(S_kv, 4), cap_elems = static_cast<int64_t>(kGemmWorkspaceCap / 8);
-  if (S_q > cap_elems / ld || B > cap_elems / (S_q * ld)) return 0;
-  const size_t one = static_cast<size_t>(round_up(B * S_q * round_up(S_kv, 4) * 4, 256));
-  return 2 * one <= kGemmWorkspaceCap ? 2 * one + 256 : 0;  // + room to align the start to 256 bytes
+  if (B <= 0 || !gemm_shape(dtype, S_q, S_kv, D_qk, D_v)) return 0;
+  const int64_t rows = gemm_rows_fitting(kGemmWorkspaceCap, B, S_q, S_kv);
+  return rows > 0 ? gemm_chunk_bytes(rows, S_q, S_kv) : 0;
 }
 
 size_t sdpa_b200_bwd_workspace_bytes(int dtype, int64_t B, int64_t S_q, int64_t S_kv, int64_t D_qk, int64_t D_v) {
@@ -269,15 +283,22 @@ static int bwd_impl(int dtype, const void* q, const void* k, const void* v, cons
   if (int r = bind_context()) return r;
   const void* ptrs[] = {q, k, v, out, d_out, dq, dk, dv};
   if (tc_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8)) return launch_bwd_tc(p, st, &t_launches);
-  const size_t extra = gemm_ws_bytes(dtype, B, S_q, S_kv, D_qk, D_v);
-  const bool gemm = extra && workspace_bytes >= delta_bytes(B, S_q) + extra;
+  // GEMM route: the rows of workspace beyond delta (a multiple of H, so a
+  // chunk of the [B/H, S, H, D] layout starts at an outer batch row)
+  int64_t rows = 0;
+  if (gemm_shape(dtype, S_q, S_kv, D_qk, D_v) && workspace_bytes > delta_bytes(B, S_q)) {
+    rows = gemm_rows_fitting(workspace_bytes - delta_bytes(B, S_q), B, S_q, S_kv);
+    rows -= rows % H;
+  }
+  const bool gemm = rows > 0;
   if (tf32_bwd_ok(dtype, S_q, S_kv, D_qk, D_v, ptrs, 8, gemm)) {
     if (gemm) {
       const uintptr_t w0 = reinterpret_cast<uintptr_t>(workspace) + delta_bytes(B, S_q);
       uint8_t* w = reinterpret_cast<uint8_t*>((w0 + 255u) & ~uintptr_t(255u));
       p.ld_k = round_up(S_kv, 4);
+      p.ws_rows = rows;
       p.ws_ds = reinterpret_cast<float*>(w);
-      p.ws_p = reinterpret_cast<float*>(w + round_up(B * S_q * p.ld_k * 4, 256));
+      p.ws_p = reinterpret_cast<float*>(w + round_up(rows * S_q * p.ld_k * 4, 256));
     }
     return launch_bwd_tf32(p, st, &t_launches);
   }

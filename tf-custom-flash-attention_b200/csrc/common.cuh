@@ -47,6 +47,7 @@ struct Params {
   float* ws_ds;
   float* ws_p;
   int64_t ld_k;
+  int64_t ws_rows;      // batch rows the workspace holds (< B: the backward runs in batch chunks)
   // fp32 forward: tiles per output fold segment, in units of the kernel's own
   // segment (default 2; SDPA_B200_TF32_FOLD, a tuning knob)
   int tf32_fold;

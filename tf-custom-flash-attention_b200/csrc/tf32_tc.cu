@@ -195,7 +195,7 @@ int sdpa_b200::launch_fwd_tf32(const Params& p, cudaStream_t st, int* launches) 
 // D_qk <= 64 on either route; D_qk = 128 on the GEMM route only (the caller
 // checks): with D_qk = 128 the resident operands and accumulators of the DQ
 // pass exceed TMEM.
-int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
+static int launch_bwd_tf32_one(const Params& p, cudaStream_t st, int* launches) {
   if (p.D_qk > 64) {
     if (!p.ws_ds) return SDPA_B200_EUNSUPPORTED;
     if (p.D_v > 64) return launch_bwd_gemm_d<128, 128>(p, st, launches);  // V lo in shared memory
@@ -204,6 +204,34 @@ int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) 
   if (p.D_v > 64) return launch_bwd_d<64, 128>(p, st, launches);
   if (p.D_v <= 32) return launch_bwd_d<64, 32>(p, st, launches);
   return launch_bwd_d<64, 64>(p, st, launches);
+}
+
+// The GEMM route with a workspace for fewer rows than the batch: chunks of
+// p.ws_rows batch rows (a multiple of H), each a complete backward of its
+// rows; every per-row quantity (tensors, stats, D, the dropout counter base
+// (b S_q + i) S_kv) is offset to the chunk's first row.
+int sdpa_b200::launch_bwd_tf32(const Params& p, cudaStream_t st, int* launches) {
+  if (!p.ws_ds || p.ws_rows >= p.B) return launch_bwd_tf32_one(p, st, launches);
+  for (int64_t b0 = 0; b0 < p.B; b0 += p.ws_rows) {
+    Params c = p;
+    c.B = p.B - b0 < p.ws_rows ? p.B - b0 : p.ws_rows;
+    const int64_t rq = b0 * p.S_q, rk = b0 * p.S_kv;  // first row of the chunk in [B*S, D] terms
+    c.q = static_cast<const float*>(p.q) + rq * p.D_qk;
+    c.k = static_cast<const float*>(p.k) + rk * p.D_qk;
+    c.v = static_cast<const float*>(p.v) + rk * p.D_v;
+    c.o = static_cast<const float*>(p.o) + rq * p.D_v;
+    c.d_o = static_cast<const float*>(p.d_o) + rq * p.D_v;
+    c.dq = static_cast<float*>(p.dq) + rq * p.D_qk;
+    c.dk = static_cast<float*>(p.dk) + rk * p.D_qk;
+    c.dv = static_cast<float*>(p.dv) + rk * p.D_v;
+    c.lse = p.lse + rq;
+    c.delta = p.delta + rq;
+    if (p.d_stats) c.d_stats = p.d_stats + rq;
+    c.rng_base = p.rng_base + static_cast<uint64_t>(rq) * static_cast<uint64_t>(p.S_kv);
+    c.ws_rows = c.B;
+    if (int r = launch_bwd_tf32_one(c, st, launches)) return r;
+  }
+  return SDPA_B200_OK;
 }
 
 SDPA_B200_STATUS_EXCHANGE(tf32)
