@@ -246,3 +246,35 @@ def test_gemm_route_in_batch_chunks_bshd():
     for name, a, b in zip(("dq", "dk", "dv"), (dq, dk, dv), g_ref):
         got = a.permute(0, 2, 1, 3).reshape(B * H, S, D).cpu().numpy()
         assert rel(got, b) <= 1e-5, (name, rel(got, b))
+
+
+def test_batch_chunks_equal_one_pass_bitwise_with_dstats():
+    """Every kernel of the GEMM route works per batch row, so chunking the batch
+    changes no bit of the result, also with a stats gradient (its rows offset
+    per chunk like D and the stats)."""
+    B, S_q, S_kv, D_qk, D_v = 5, 100, 140, 64, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, S_q, D_qk, generator=g, device="cuda") * 0.5
+    k = torch.randn(B, S_kv, D_qk, generator=g, device="cuda") * 0.5
+    v = torch.randn(B, S_kv, D_v, generator=g, device="cuda") * 0.5
+    do = torch.randn(B, S_q, D_v, generator=g, device="cuda")
+    dst = torch.randn(B, S_q, generator=g, device="cuda") * 0.1
+    o, s = fa.sdpa(q, k, v, 5, 9, scale=0.125, dropout=0.1)
+    L = fa._lib.lib()
+
+    def run(n):
+        ws = torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        rc = L.sdpa_b200_bwd_dstats(fa._lib.F32, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), s.data_ptr(),
+                                    dst.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S_q,
+                                    S_kv, D_qk, D_v, 0.125, 0.1, 0, 5, 9, ws.data_ptr(), n,
+                                    torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, fa._lib.strerror(rc)
+        return fa.last_launch_count(), (dq, dk, dv)
+
+    n_full, full = run(L.sdpa_b200_bwd_workspace_bytes(fa._lib.F32, B, S_q, S_kv, D_qk, D_v))
+    n_chunk, chunked = run(_chunk_ws_bytes(B, S_q, S_kv, 2))
+    assert (n_full, n_chunk) == (5, 15)
+    torch.cuda.synchronize()
+    for a, b in zip(full, chunked):
+        assert torch.equal(a, b)
